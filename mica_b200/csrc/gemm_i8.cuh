@@ -1,0 +1,417 @@
+// gemm_i8.cuh -- W8A8 GEMM for sm_100a on tcgen05 tensor cores.
+//
+//   C[m, n] = epilogue( sum_k A[m, k] * B[n, k] )      A int8 [M, K], B int8 [N, K] (K-major)
+//
+// One persistent CTA per SM walks output tiles of 128 x BN. Warp roles:
+//   warp 0      TMA producer: 128 x 128-byte A and BN x 128-byte B tiles into a ring of
+//               shared-memory stages (128-byte swizzle), completion on mbarriers;
+//   warp 1      tensor-memory owner and MMA issuer: four tcgen05.mma.kind::i8 (128 x BN x 32)
+//               per stage into an int32 accumulator in TMEM, double-buffered (2 x BN columns)
+//               so the epilogue of tile i overlaps the main loop of tile i+1;
+//   warps 2..5  epilogue: tcgen05.ld 32 lanes x 32 columns, fp32 dequant (and SwiGLU),
+//               16-bit/fp32 pack into a swizzled shared tile, TMA store per 32-row box.
+// Every wait is bounded (common.cuh); a wait that runs out unwinds the CTA.
+//
+// Reference semantics: v0.5/serving/kernel_src/kernels.py:41-69 (mm_i8): int32 accumulate,
+// y = acc * SA[m] * SB[n] (+ BIAS[n]) evaluated left to right in fp32, cast to the output type.
+#pragma once
+
+#include "common.cuh"
+
+namespace mica {
+
+enum EpiKind { EPI_DEQUANT = 0, EPI_SWIGLU = 1 };
+
+template <int BN_>
+struct GemmShape {
+    static constexpr int BM = 128;
+    static constexpr int BN = BN_;
+    static constexpr int BK = 128;                      // bytes (= int8 elements) of K per stage
+    static constexpr int UMMA_K = 32;                   // K of one kind::i8 MMA
+    static constexpr int A_BYTES = BM * BK;             // 16 KB
+    static constexpr int B_BYTES = BN * BK;
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int EPI_WARPS = 4;
+    static constexpr int BOX_BYTES = 32 * 128;          // one 32-row x 128-byte store box
+    static constexpr int EPI_BYTES = EPI_WARPS * 2 * BOX_BYTES;
+    static constexpr int AUX_BYTES = 256;               // mbarriers, TMEM address, abort flag
+    static constexpr int SMEM_OPTIN = 232448;           // sm_100 opt-in shared memory per block
+    static constexpr int STAGES_RAW = (SMEM_OPTIN - 1024 - EPI_BYTES - AUX_BYTES) / STAGE_BYTES;
+    static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
+    static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + AUX_BYTES;
+    static constexpr int ACC_COLS = BN;                 // int32 accumulator columns per buffer
+    static constexpr int TMEM_COLS = (2 * BN < 32) ? 32 : 2 * BN;
+    static constexpr int THREADS = 192;
+    static_assert(STAGES >= 2, "not enough shared memory for a pipeline");
+    static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256, "BN");
+    static_assert(SMEM_BYTES <= SMEM_OPTIN, "smem");
+};
+
+struct GemmArgs {
+    const float* sa;      // [M] token scales
+    const float* sb;      // [N] channel scales
+    const float* bias;    // [N] or nullptr
+    int M, N, K;
+    int round_mode;       // swiglu: rounding of the fused requantisation
+    // swiglu only
+    unsigned* row_amax;   // [M] float bits of max |h|
+    unsigned* grid_sync;  // grid barrier counter (zeroed before launch)
+    const __nv_bfloat16* h;  // [M, I] (read back in phase 2)
+    long ldh;
+    int8_t* q_out;        // [M, I]
+    long ldq;
+    float* s_out;         // [M]
+};
+
+__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&v);
+}
+__device__ __forceinline__ uint32_t pack_f16(float a, float b) {
+    __half2 v = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&v);
+}
+__device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d)
+                 : "memory");
+}
+
+template <int BN, int EPI, typename OutT>
+__global__ void __launch_bounds__(192, 1)
+gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+               const __grid_constant__ CUtensorMap tmap_c, const GemmArgs args) {
+    using S = GemmShape<BN>;
+    constexpr int STAGES = S::STAGES;
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    extern __shared__ uint8_t smem_raw[];
+    // 1024-byte alignment: the 128-byte swizzle pattern is a function of address bits [4,10).
+    const uint32_t raw_addr = smem_u32(smem_raw);
+    uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+    uint8_t* smem_a = smem;                                   // STAGES x A_BYTES
+    uint8_t* smem_b = smem + STAGES * S::A_BYTES;             // STAGES x B_BYTES
+    uint8_t* smem_epi = smem_b + STAGES * S::B_BYTES;         // 4 warps x 2 boxes
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem_epi + S::EPI_BYTES);
+    uint64_t* full_bar = bars;                                // [STAGES]  TMA -> MMA
+    uint64_t* empty_bar = bars + STAGES;                      // [STAGES]  MMA -> TMA
+    uint64_t* tfull_bar = bars + 2 * STAGES;                  // [2]       MMA -> epilogue
+    uint64_t* tempty_bar = bars + 2 * STAGES + 2;             // [2]       epilogue -> MMA
+    uint64_t* drain_bar = bars + 2 * STAGES + 4;              // [1]       teardown
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
+    volatile uint32_t* abort_flag = tmem_slot + 1;
+
+    const int M = args.M, N = args.N, K = args.K;
+    const int num_m = (M + S::BM - 1) / S::BM;
+    const int num_n = (N + BN - 1) / BN;
+    const int num_tiles = num_m * num_n;
+    const int num_kb = (K + S::BK - 1) / S::BK;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < STAGES; ++i) {
+            mbar_init(&full_bar[i], 1);
+            mbar_init(&empty_bar[i], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&tfull_bar[i], 1);
+            mbar_init(&tempty_bar[i], S::EPI_WARPS * 32);
+        }
+        mbar_init(drain_bar, 1);
+        *abort_flag = 0u;
+        fence_mbar_init();
+        tma_prefetch_desc(&tmap_a);
+        tma_prefetch_desc(&tmap_b);
+        tma_prefetch_desc(&tmap_c);
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, S::TMEM_COLS);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ------------------------------- TMA producer -------------------------------
+        if (lane == 0) {
+            uint32_t it = 0;  // k-blocks issued so far (stage = it % STAGES)
+            bool ok = true;
+            const uint64_t pol_b = policy_evict_last();   // weights: re-read by every M block
+            for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+                const int m0 = (tile / num_n) * S::BM;
+                const int n0 = (tile % num_n) * BN;
+                for (int kb = 0; kb < num_kb; ++kb, ++it) {
+                    const int st = it % STAGES;
+                    const uint32_t ph = (it / STAGES) & 1u;
+                    if (!mbar_wait(&empty_bar[st], ph ^ 1u, abort_flag, MICA_DEV_TIMEOUT_PRODUCER)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&full_bar[st], S::STAGE_BYTES);
+                    tma_load_2d(smem_a + st * S::A_BYTES, &tmap_a, &full_bar[st], kb * S::BK, m0);
+                    tma_load_2d_hint(smem_b + st * S::B_BYTES, &tmap_b, &full_bar[st], kb * S::BK, n0, pol_b);
+                }
+            }
+            // Drain: the last loads of each stage must land before this CTA's smem goes away.
+            const uint32_t first = it > static_cast<uint32_t>(STAGES) ? it - STAGES : 0u;
+            for (uint32_t j = first; j < it; ++j) {
+                mbar_wait(&full_bar[j % STAGES], (j / STAGES) & 1u, abort_flag, MICA_DEV_TIMEOUT_DRAIN);
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        // ------------------------------- MMA issuer ---------------------------------
+        constexpr uint32_t idesc = idesc_i8(S::BM, BN);
+        const uint32_t a_base = smem_u32(smem_a);
+        const uint32_t b_base = smem_u32(smem_b);
+        uint32_t it = 0;
+        int local = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
+            const int acc = local & 1;
+            const uint32_t acc_ph = (local >> 1) & 1;
+            bool w = true;
+            if (lane == 0) w = mbar_wait(&tempty_bar[acc], acc_ph ^ 1u, abort_flag, MICA_DEV_TIMEOUT_MMA);
+            if (!__shfl_sync(0xffffffffu, w, 0)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t d_tmem = tmem_base + acc * S::ACC_COLS;
+            for (int kb = 0; kb < num_kb; ++kb, ++it) {
+                const int st = it % STAGES;
+                const uint32_t ph = (it / STAGES) & 1u;
+                if (lane == 0) w = mbar_wait(&full_bar[st], ph, abort_flag, MICA_DEV_TIMEOUT_MMA);
+                if (!__shfl_sync(0xffffffffu, w, 0)) { ok = false; break; }
+                tc_fence_after();
+                if (lane == 0) {
+                    const uint32_t a_addr = a_base + st * S::A_BYTES;
+                    const uint32_t b_addr = b_base + st * S::B_BYTES;
+#pragma unroll
+                    for (int k = 0; k < S::BK / S::UMMA_K; ++k) {
+                        mma_i8(d_tmem, smem_desc_k128(a_addr + k * S::UMMA_K), smem_desc_k128(b_addr + k * S::UMMA_K),
+                               idesc, (kb | k) != 0 ? 1u : 0u);
+                    }
+                    mma_commit(&empty_bar[st]);          // frees the stage when these MMAs finish
+                    if (kb == num_kb - 1) mma_commit(&tfull_bar[acc]);  // accumulator complete
+                }
+                __syncwarp();
+            }
+        }
+        // Drain: every MMA issued must finish before tensor memory is released.
+        if (lane == 0) {
+            mma_commit(drain_bar);
+            mbar_wait(drain_bar, 0, abort_flag, MICA_DEV_TIMEOUT_DRAIN);
+        }
+        __syncwarp();
+    } else {
+        // ------------------------------- epilogue -----------------------------------
+        const int q4 = warp & 3;                  // TMEM lane quarter this warp may access
+        const int row_local = q4 * 32 + lane;
+        const int ew = warp - 2;                  // epilogue warp 0..3
+        uint8_t* my_boxes = smem_epi + ew * 2 * S::BOX_BYTES;
+        int box_count = 0;
+        int local = 0;
+        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+            const int m0 = (tile / num_n) * S::BM;
+            const int n0 = (tile % num_n) * BN;
+            const int acc = local & 1;
+            const uint32_t acc_ph = (local >> 1) & 1;
+            bool w = true;
+            if (lane == 0) w = mbar_wait(&tfull_bar[acc], acc_ph, abort_flag, MICA_DEV_TIMEOUT_EPILOGUE);
+            if (!__shfl_sync(0xffffffffu, w, 0)) break;
+            tc_fence_after();
+
+            const int grow = m0 + row_local;
+            const float sa_v = grow < M ? args.sa[grow] : 0.f;
+            const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q4 * 32) << 16) + acc * S::ACC_COLS;
+
+            if constexpr (EPI == EPI_DEQUANT) {
+                constexpr int COLS_PER_BOX = 128 / static_cast<int>(sizeof(OutT));
+                constexpr int CHUNKS_PER_BOX = COLS_PER_BOX / 32;
+                constexpr int BOXES = BN / COLS_PER_BOX;
+#pragma unroll 1
+                for (int bx = 0; bx < BOXES; ++bx, ++box_count) {
+                    uint8_t* box = my_boxes + (box_count & 1) * S::BOX_BYTES;
+                    if (lane == 0) tma_store_wait_read<1>();   // the store that used this box is done reading
+                    __syncwarp();
+                    const uint32_t box_row = smem_u32(box) + lane * 128;
+#pragma unroll
+                    for (int cc = 0; cc < CHUNKS_PER_BOX; ++cc) {
+                        const int col0 = bx * COLS_PER_BOX + cc * 32;
+                        const int gcol = n0 + col0 + lane;
+                        const float sb_l = gcol < N ? args.sb[gcol] : 0.f;
+                        const float bias_l = (args.bias != nullptr && gcol < N) ? args.bias[gcol] : 0.f;
+                        uint32_t r[32];
+                        tmem_ld_32x32b_x32(t_row + col0, r);
+                        tmem_ld_wait();
+                        float y[32];
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            const float sbj = __shfl_sync(0xffffffffu, sb_l, j);
+                            y[j] = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[j])), sa_v), sbj);
+                        }
+                        if (args.bias != nullptr) {
+#pragma unroll
+                            for (int j = 0; j < 32; ++j) y[j] = __fadd_rn(y[j], __shfl_sync(0xffffffffu, bias_l, j));
+                        }
+                        if constexpr (sizeof(OutT) == 2) {
+                            uint32_t p[16];
+#pragma unroll
+                            for (int j = 0; j < 16; ++j) {
+                                if constexpr (std::is_same<OutT, __half>::value) p[j] = pack_f16(y[2 * j], y[2 * j + 1]);
+                                else p[j] = pack_bf16(y[2 * j], y[2 * j + 1]);
+                            }
+#pragma unroll
+                            for (int c = 0; c < 4; ++c) {
+                                const int chunk = cc * 4 + c;
+                                st_shared_v4(box_row + ((chunk ^ (lane & 7)) << 4), p[4 * c], p[4 * c + 1],
+                                             p[4 * c + 2], p[4 * c + 3]);
+                            }
+                        } else {
+#pragma unroll
+                            for (int c = 0; c < 8; ++c) {
+                                st_shared_v4(box_row + ((c ^ (lane & 7)) << 4), __float_as_uint(y[4 * c]),
+                                             __float_as_uint(y[4 * c + 1]), __float_as_uint(y[4 * c + 2]),
+                                             __float_as_uint(y[4 * c + 3]));
+                            }
+                        }
+                    }
+                    if (bx == BOXES - 1) {
+                        // accumulator fully read: hand the buffer back to the MMA warp
+                        tc_fence_before();
+                        mbar_arrive(&tempty_bar[acc]);
+                    }
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_store_2d(&tmap_c, box, n0 + bx * COLS_PER_BOX, m0 + q4 * 32);
+                        tma_store_commit();
+                    }
+                }
+            } else {
+                // SwiGLU: each 32-column chunk holds 16 gate and 16 up columns of the same
+                // 16 outputs; h = bf16(bf16(silu(g)) * u), running max |h| per row.
+                constexpr int H_PER_BOX = 64;                 // bf16 h columns per 128-byte box row
+                constexpr int CHUNKS_PER_BOX = 4;             // 4 x 16 h columns
+                constexpr int BOXES = BN / 128;
+                float amax = 0.f;
+#pragma unroll 1
+                for (int bx = 0; bx < BOXES; ++bx, ++box_count) {
+                    uint8_t* box = my_boxes + (box_count & 1) * S::BOX_BYTES;
+                    if (lane == 0) tma_store_wait_read<1>();
+                    __syncwarp();
+                    const uint32_t box_row = smem_u32(box) + lane * 128;
+#pragma unroll
+                    for (int cc = 0; cc < CHUNKS_PER_BOX; ++cc) {
+                        const int col0 = bx * 128 + cc * 32;
+                        const int gcol = n0 + col0 + lane;
+                        const float sb_l = gcol < N ? args.sb[gcol] : 0.f;
+                        const float bias_l = (args.bias != nullptr && gcol < N) ? args.bias[gcol] : 0.f;
+                        uint32_t r[32];
+                        tmem_ld_32x32b_x32(t_row + col0, r);
+                        tmem_ld_wait();
+                        uint32_t p[8];
+#pragma unroll
+                        for (int j = 0; j < 16; j += 2) {
+                            float hv[2];
+#pragma unroll
+                            for (int e = 0; e < 2; ++e) {
+                                const int jj = j + e;
+                                float g = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[jj])), sa_v),
+                                                    __shfl_sync(0xffffffffu, sb_l, jj));
+                                float u = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[16 + jj])), sa_v),
+                                                    __shfl_sync(0xffffffffu, sb_l, 16 + jj));
+                                if (args.bias != nullptr) {
+                                    g = __fadd_rn(g, __shfl_sync(0xffffffffu, bias_l, jj));
+                                    u = __fadd_rn(u, __shfl_sync(0xffffffffu, bias_l, 16 + jj));
+                                }
+                                g = bf16_round(g);
+                                u = bf16_round(u);
+                                const float act = bf16_round(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))));
+                                const float h = bf16_round(__fmul_rn(act, u));
+                                amax = fmaxf(amax, fabsf(h));
+                                hv[e] = h;
+                            }
+                            p[j / 2] = pack_bf16(hv[0], hv[1]);
+                        }
+#pragma unroll
+                        for (int c = 0; c < 2; ++c) {
+                            const int chunk = cc * 2 + c;
+                            st_shared_v4(box_row + ((chunk ^ (lane & 7)) << 4), p[4 * c], p[4 * c + 1], p[4 * c + 2],
+                                         p[4 * c + 3]);
+                        }
+                    }
+                    if (bx == BOXES - 1) {
+                        tc_fence_before();
+                        mbar_arrive(&tempty_bar[acc]);
+                    }
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_store_2d(&tmap_c, box, n0 / 2 + bx * H_PER_BOX, m0 + q4 * 32);
+                        tma_store_commit();
+                    }
+                }
+                if (grow < M) atomicMax(args.row_amax + grow, __float_as_uint(amax));
+            }
+        }
+        // all stores must be complete (not only read) before the grid-wide phase or exit
+        if (lane == 0) tma_store_wait_all<0>();
+        __syncwarp();
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_free(tmem_base, S::TMEM_COLS);
+    }
+
+    if constexpr (EPI == EPI_SWIGLU) {
+        // ---- phase 2: per-token requantisation of h once every row max is final ----
+        // Grid barrier (all CTAs are co-resident: cooperative launch, one CTA per SM).
+        if (threadIdx.x == 0) {
+            fence_proxy_async_global();
+            __threadfence();
+            atomicAdd(args.grid_sync, 1u);
+            const unsigned target = gridDim.x;
+            const unsigned long long t0 = global_ns();
+            for (uint32_t it = 0;; ++it) {
+                unsigned v;
+                asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(args.grid_sync) : "memory");
+                if (v >= target) break;
+                if ((it & 15u) == 15u && global_ns() - t0 > kWaitLimitNs) {
+                    *abort_flag = 1u;
+                    atomicExch(&g_dev_error, MICA_DEV_TIMEOUT_GRID);
+                    break;
+                }
+                __nanosleep(64);
+            }
+            __threadfence();
+        }
+        __syncthreads();
+        if (*abort_flag) return;
+        const int I = N / 2;
+        const int warps_total = gridDim.x * (blockDim.x >> 5);
+        for (int row = blockIdx.x * (blockDim.x >> 5) + warp; row < M; row += warps_total) {
+            const unsigned bits = __ldcg(args.row_amax + row);
+            const float scale = __fdiv_rn(fmaxf(__uint_as_float(bits), 1e-8f), 127.0f);
+            const __nv_bfloat16* hrow = args.h + static_cast<long>(row) * args.ldh;
+            int8_t* qrow = args.q_out + static_cast<long>(row) * args.ldq;
+            for (int c = lane * 8; c < I; c += 32 * 8) {
+                const uint4 v = __ldcg(reinterpret_cast<const uint4*>(hrow + c));
+                const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+                uint32_t out[2] = {0u, 0u};
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    const uint32_t half = (w4[e >> 1] >> ((e & 1) * 16)) & 0xFFFFu;
+                    const float x = __uint_as_float(half << 16);
+                    const int qv = quant_round(__fdiv_rn(x, scale), args.round_mode);
+                    out[e >> 2] |= (static_cast<uint32_t>(qv) & 0xFFu) << ((e & 3) * 8);
+                }
+                *reinterpret_cast<uint2*>(qrow + c) = make_uint2(out[0], out[1]);
+            }
+            if (lane == 0) args.s_out[row] = scale;
+        }
+    }
+}
+
+}  // namespace mica

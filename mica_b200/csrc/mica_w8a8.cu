@@ -1,0 +1,458 @@
+// mica_w8a8.cu -- the single translation unit of libmica_w8a8.so: kernels (included
+// headers) and the extern "C" entry points declared in include/mica_w8a8.h.
+//
+// Host side: argument and alignment checks that return status codes (the reference's
+// launcher turns the same conditions into `None` misses, v0.5/serving/lib/
+// int8_kernels.py:268-311, :325-406), TMA descriptor encoding, tile choice and launch.
+#include <type_traits>
+#include <cudaTypedefs.h>
+
+#include <atomic>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "common.cuh"
+#include "gemm_i8.cuh"
+#include "quant.cuh"
+#include "readout.cuh"
+
+using namespace mica;
+
+// ======================================================================================
+// host helpers
+// ======================================================================================
+namespace mica_host {
+
+static thread_local char t_err[256] = {0};
+
+void set_cuda_error(cudaError_t e) {
+    snprintf(t_err, sizeof(t_err), "%s: %s", cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+constexpr int kMaxDev = 64;
+struct DevInfo {
+    std::atomic<int> state{0};  // 0 unknown, 1 ok, 2 unsupported
+    int sm_count = 0;
+    int smem_optin = 0;
+};
+static DevInfo g_dev[kMaxDev];
+static std::mutex g_lock;
+
+int check_device(int* sm_count) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) { set_cuda_error(e); return MICA_ERR_CUDA; }
+    if (dev < 0 || dev >= kMaxDev) return MICA_ERR_ARCH;
+    DevInfo& d = g_dev[dev];
+    int st = d.state.load(std::memory_order_acquire);
+    if (st == 0) {
+        std::lock_guard<std::mutex> g(g_lock);
+        st = d.state.load(std::memory_order_relaxed);
+        if (st == 0) {
+            int major = 0, minor = 0, sms = 0, optin = 0;
+            if ((e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev)) != cudaSuccess ||
+                (e = cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev)) != cudaSuccess ||
+                (e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess ||
+                (e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev)) != cudaSuccess) {
+                set_cuda_error(e);
+                return MICA_ERR_CUDA;
+            }
+            d.sm_count = sms;
+            d.smem_optin = optin;
+            // sm_100a code runs on compute capability 10.0 only.
+            st = (major == 10 && minor == 0 && optin >= 232448) ? 1 : 2;
+            d.state.store(st, std::memory_order_release);
+        }
+    }
+    if (st != 1) return MICA_ERR_ARCH;
+    if (sm_count) *sm_count = d.sm_count;
+    return MICA_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+static std::once_flag g_encode_once;
+
+int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, uint64_t inner, uint64_t outer,
+                 uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer) {
+    std::call_once(g_encode_once, [] {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    });
+    if (!g_encode) {
+        snprintf(t_err, sizeof(t_err), "cuTensorMapEncodeTiled entry point not found");
+        return MICA_ERR_CUDA;
+    }
+    const cuuint64_t dims[2] = {inner, outer};
+    const cuuint64_t strides[1] = {row_bytes};
+    const cuuint32_t box[2] = {box_inner, box_outer};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = g_encode(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        snprintf(t_err, sizeof(t_err), "cuTensorMapEncodeTiled failed: CUresult %d", static_cast<int>(r));
+        return MICA_ERR_CUDA;
+    }
+    return MICA_OK;
+}
+
+static int launch_status() {
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) { set_cuda_error(e); return MICA_ERR_CUDA; }
+    return MICA_OK;
+}
+
+static size_t dt_size(int dt) { return dt == MICA_DT_FP32 ? 4 : 2; }
+
+// ---- GEMM kernel registry ------------------------------------------------------------
+template <int BN, int EPI, typename OutT>
+static int gemm_prepare() {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    static std::atomic<uint64_t> done{0};  // one bit per device
+    const uint64_t bit = 1ull << (dev & 63);
+    if (done.load(std::memory_order_acquire) & bit) return MICA_OK;
+    cudaError_t e = cudaFuncSetAttribute(gemm_i8_kernel<BN, EPI, OutT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         GemmShape<BN>::SMEM_BYTES);
+    if (e != cudaSuccess) { set_cuda_error(e); return MICA_ERR_CUDA; }
+    done.fetch_or(bit, std::memory_order_release);
+    return MICA_OK;
+}
+
+template <int BN, int EPI, typename OutT>
+static int gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const GemmArgs& args,
+                       int grid, bool cooperative, cudaStream_t stream) {
+    int rc = gemm_prepare<BN, EPI, OutT>();
+    if (rc) return rc;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(GemmShape<BN>::THREADS);
+    cfg.dynamicSmemBytes = GemmShape<BN>::SMEM_BYTES;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    if (cooperative) {
+        attr[0].id = cudaLaunchAttributeCooperative;
+        attr[0].val.cooperative = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+    }
+    cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_i8_kernel<BN, EPI, OutT>, ta, tb, tc, args);
+    if (e != cudaSuccess) { set_cuda_error(e); return MICA_ERR_CUDA; }
+    return launch_status();
+}
+
+// Tile choice: the widest tile that still gives every SM work; a pinned table in the
+// Python layer may override it (mica_w8a8_gemm_cfg).
+static int pick_bn(int M, int N, int sms) {
+    const long m_blocks = (M + 127) / 128;
+    const long t256 = m_blocks * ((N + 255) / 256);
+    const long t128 = m_blocks * ((N + 127) / 128);
+    if (t256 >= 2L * sms) return 256;
+    if (t128 >= sms) return 128;
+    return 64;
+}
+
+}  // namespace mica_host
+
+using namespace mica_host;
+
+// ======================================================================================
+// entry points (C linkage comes from their declarations in include/mica_w8a8.h)
+// ======================================================================================
+
+const char* mica_last_cuda_error(void) { return t_err; }
+
+int mica_query(int device, mica_caps* caps) {
+    if (!caps) return MICA_ERR_ARG;
+    memset(caps, 0, sizeof(*caps));
+    caps->device = device;
+    caps->abi_version = MICA_ABI_VERSION;
+    int n = 0;
+    cudaError_t e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess) { set_cuda_error(e); return MICA_ERR_CUDA; }
+    if (device < 0 || device >= n) return MICA_ERR_ARG;
+    if ((e = cudaDeviceGetAttribute(&caps->cc_major, cudaDevAttrComputeCapabilityMajor, device)) != cudaSuccess ||
+        (e = cudaDeviceGetAttribute(&caps->cc_minor, cudaDevAttrComputeCapabilityMinor, device)) != cudaSuccess ||
+        (e = cudaDeviceGetAttribute(&caps->sm_count, cudaDevAttrMultiProcessorCount, device)) != cudaSuccess ||
+        (e = cudaDeviceGetAttribute(&caps->max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device)) !=
+            cudaSuccess) {
+        set_cuda_error(e);
+        return MICA_ERR_CUDA;
+    }
+    caps->supported = (caps->cc_major == 10 && caps->cc_minor == 0 && caps->max_smem_optin >= 232448) ? 1 : 0;
+    return MICA_OK;
+}
+
+int mica_preload(int* n_kernels) {
+    int rc = check_device(nullptr);
+    if (rc) return rc;
+    int n = 0;
+#define PREP(BN, EPI, T)                                  \
+    if ((rc = gemm_prepare<BN, EPI, T>()) != MICA_OK) return rc; \
+    ++n;
+    PREP(64, EPI_DEQUANT, __nv_bfloat16)
+    PREP(128, EPI_DEQUANT, __nv_bfloat16)
+    PREP(256, EPI_DEQUANT, __nv_bfloat16)
+    PREP(64, EPI_DEQUANT, __half)
+    PREP(128, EPI_DEQUANT, __half)
+    PREP(256, EPI_DEQUANT, __half)
+    PREP(64, EPI_DEQUANT, float)
+    PREP(128, EPI_DEQUANT, float)
+    PREP(256, EPI_DEQUANT, float)
+    PREP(128, EPI_SWIGLU, __nv_bfloat16)
+    PREP(256, EPI_SWIGLU, __nv_bfloat16)
+#undef PREP
+    if (n_kernels) *n_kernels = n;
+    return MICA_OK;
+}
+
+int mica_device_error(int* code, void* stream) {
+    if (!code) return MICA_ERR_ARG;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) { set_cuda_error(e); return MICA_ERR_CUDA; }
+    int v = 0;
+    if ((e = cudaMemcpyFromSymbol(&v, g_dev_error, sizeof(int))) != cudaSuccess) { set_cuda_error(e); return MICA_ERR_CUDA; }
+    const int zero = 0;
+    if ((e = cudaMemcpyToSymbol(g_dev_error, &zero, sizeof(int))) != cudaSuccess) { set_cuda_error(e); return MICA_ERR_CUDA; }
+    *code = v;
+    return MICA_OK;
+}
+
+// ---------------------------------------------------------------------------------------
+static int quant_launch(const QuantArgs& a, int dtype, bool norm, cudaStream_t st) {
+    const int nvec = a.K / 8;
+    int threads = ((nvec + QV - 1) / QV + 31) / 32 * 32;
+    if (threads < 32) threads = 32;
+    if (threads > 1024) return MICA_ERR_UNSUPPORTED;
+    const dim3 grid(a.M), block(threads);
+    if (dtype == MICA_DT_BF16) {
+        if (norm) quant_rows_kernel<__nv_bfloat16, true><<<grid, block, 0, st>>>(a);
+        else quant_rows_kernel<__nv_bfloat16, false><<<grid, block, 0, st>>>(a);
+    } else if (dtype == MICA_DT_FP16) {
+        if (norm) quant_rows_kernel<__half, true><<<grid, block, 0, st>>>(a);
+        else quant_rows_kernel<__half, false><<<grid, block, 0, st>>>(a);
+    } else {
+        if (norm) return MICA_ERR_ARG;
+        quant_rows_kernel<float, false><<<grid, block, 0, st>>>(a);
+    }
+    return launch_status();
+}
+
+int mica_act_quant(const void* x, int x_dtype, long ldx, const float* inv, int8_t* q, long ldq, float* s, int M,
+                   int K, int round_mode, void* stream) {
+    if (!x || !q || !s || x_dtype < 0 || x_dtype > 2 || (round_mode != 0 && round_mode != 1)) return MICA_ERR_ARG;
+    if (M < 0 || K < 8 || (K & 7) || ldx < K || ldq < K) return MICA_ERR_SHAPE;
+    if (static_cast<long>(M) * (ldx > ldq ? ldx : ldq) >= (1L << 40)) return MICA_ERR_RANGE;
+    const size_t es = dt_size(x_dtype);
+    if (!aligned16(x) || !aligned16(q) || (inv && !aligned16(inv)) || (ldx * es) % 16 || ldq % 16) return MICA_ERR_ALIGN;
+    int rc = check_device(nullptr);
+    if (rc) return rc;
+    if (M == 0) return MICA_OK;
+    QuantArgs a = {};
+    a.x = x; a.ldx = ldx; a.inv = inv; a.q = q; a.ldq = ldq; a.s = s;
+    a.M = M; a.K = K; a.round_mode = round_mode;
+    return quant_launch(a, x_dtype, false, static_cast<cudaStream_t>(stream));
+}
+
+int mica_rmsnorm_quant(const void* x, int x_dtype, long ldx, const void* residual, long ldr, const void* gamma,
+                       int norm_style, float eps, const float* inv, void* y_out, long ldy, void* sum_out, long ldsum,
+                       int8_t* q, long ldq, float* s, int M, int K, int round_mode, void* stream) {
+    if (!x || !gamma || (!q != !s) || (!q && !y_out) || (x_dtype != MICA_DT_BF16 && x_dtype != MICA_DT_FP16) ||
+        (round_mode != 0 && round_mode != 1) || (norm_style != MICA_NORM_OFFSET && norm_style != MICA_NORM_WEIGHT))
+        return MICA_ERR_ARG;
+    if (M < 0 || K < 8 || (K & 7) || ldx < K || (q && ldq < K) || (residual && ldr < K) || (y_out && ldy < K) ||
+        (sum_out && ldsum < K))
+        return MICA_ERR_SHAPE;
+    if (sum_out && !residual) return MICA_ERR_ARG;
+    const long es = 2;
+    if (!aligned16(x) || !aligned16(gamma) || (q && !aligned16(q)) || (inv && !aligned16(inv)) ||
+        (residual && (!aligned16(residual) || (ldr * es) % 16)) || (y_out && (!aligned16(y_out) || (ldy * es) % 16)) ||
+        (sum_out && (!aligned16(sum_out) || (ldsum * es) % 16)) || (ldx * es) % 16 || ldq % 16)
+        return MICA_ERR_ALIGN;
+    int rc = check_device(nullptr);
+    if (rc) return rc;
+    if (M == 0) return MICA_OK;
+    QuantArgs a = {};
+    a.x = x; a.ldx = ldx; a.residual = residual; a.ldr = ldr; a.gamma = gamma; a.norm_style = norm_style;
+    a.eps = eps; a.inv = inv; a.y_out = y_out; a.ldy = ldy; a.sum_out = sum_out; a.ldsum = ldsum;
+    a.q = q; a.ldq = ldq; a.s = s; a.M = M; a.K = K; a.round_mode = round_mode;
+    return quant_launch(a, x_dtype, true, static_cast<cudaStream_t>(stream));
+}
+
+// ---------------------------------------------------------------------------------------
+static int gemm_checks(const int8_t* A, long lda, const int8_t* B, long ldb, const float* sa, const float* sb,
+                       const float* bias, const void* C, int c_dtype, long ldc, int M, int N, int K) {
+    if (!A || !B || !sa || !sb || !C || c_dtype < 0 || c_dtype > 2) return MICA_ERR_ARG;
+    if (M < 0 || N < 1 || K < 16 || (K & 15) || lda < K || ldb < K || ldc < N) return MICA_ERR_SHAPE;
+    if (M > (1 << 30) || N > (1 << 30) || K > (1 << 30)) return MICA_ERR_RANGE;
+    const long es = static_cast<long>(dt_size(c_dtype));
+    if (!aligned16(A) || !aligned16(B) || !aligned16(C) || lda % 16 || ldb % 16 || (ldc * es) % 16)
+        return MICA_ERR_ALIGN;
+    (void)sa; (void)sb; (void)bias;
+    return MICA_OK;
+}
+
+template <int BN>
+static int gemm_dispatch_out(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const GemmArgs& g,
+                             int c_dtype, int grid, cudaStream_t st) {
+    if (c_dtype == MICA_DT_BF16) return gemm_launch<BN, EPI_DEQUANT, __nv_bfloat16>(ta, tb, tc, g, grid, false, st);
+    if (c_dtype == MICA_DT_FP16) return gemm_launch<BN, EPI_DEQUANT, __half>(ta, tb, tc, g, grid, false, st);
+    return gemm_launch<BN, EPI_DEQUANT, float>(ta, tb, tc, g, grid, false, st);
+}
+
+int mica_w8a8_gemm_cfg(const int8_t* A, long lda, const int8_t* B, long ldb, const float* sa, const float* sb,
+                       const float* bias, void* C, int c_dtype, long ldc, int M, int N, int K, int block_n,
+                       int max_ctas, void* stream) {
+    int rc = gemm_checks(A, lda, B, ldb, sa, sb, bias, C, c_dtype, ldc, M, N, K);
+    if (rc) return rc;
+    if (block_n != 0 && block_n != 64 && block_n != 128 && block_n != 256) return MICA_ERR_ARG;
+    if (max_ctas < 0) return MICA_ERR_ARG;
+    int sms = 0;
+    if ((rc = check_device(&sms))) return rc;
+    if (M == 0) return MICA_OK;
+    const int bn = block_n ? block_n : pick_bn(M, N, sms);
+    CUtensorMap ta, tb, tc;
+    const CUtensorMapDataType cdt = c_dtype == MICA_DT_BF16   ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                    : c_dtype == MICA_DT_FP16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                              : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+    const uint32_t es = static_cast<uint32_t>(dt_size(c_dtype));
+    if ((rc = make_tmap_2d(&ta, A, CU_TENSOR_MAP_DATA_TYPE_UINT8, K, M, lda, 128, 128)) ||
+        (rc = make_tmap_2d(&tb, B, CU_TENSOR_MAP_DATA_TYPE_UINT8, K, N, ldb, 128, bn)) ||
+        (rc = make_tmap_2d(&tc, C, cdt, N, M, ldc * es, 128 / es, 32)))
+        return rc;
+    GemmArgs g = {};
+    g.sa = sa; g.sb = sb; g.bias = bias; g.M = M; g.N = N; g.K = K;
+    const long tiles = static_cast<long>((M + 127) / 128) * ((N + bn - 1) / bn);
+    int grid = static_cast<int>(tiles < sms ? tiles : sms);
+    if (max_ctas > 0 && grid > max_ctas) grid = max_ctas;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (bn == 256) return gemm_dispatch_out<256>(ta, tb, tc, g, c_dtype, grid, st);
+    if (bn == 128) return gemm_dispatch_out<128>(ta, tb, tc, g, c_dtype, grid, st);
+    return gemm_dispatch_out<64>(ta, tb, tc, g, c_dtype, grid, st);
+}
+
+int mica_w8a8_gemm(const int8_t* A, long lda, const int8_t* B, long ldb, const float* sa, const float* sb,
+                   const float* bias, void* C, int c_dtype, long ldc, int M, int N, int K, void* stream) {
+    return mica_w8a8_gemm_cfg(A, lda, B, ldb, sa, sb, bias, C, c_dtype, ldc, M, N, K, 0, 0, stream);
+}
+
+// ---------------------------------------------------------------------------------------
+// workspace layout: [row_amax: M uint32, padded to 16 B][grid counter: 16 B]
+size_t mica_swiglu_workspace_bytes(int M) {
+    if (M < 0) return 0;
+    return (static_cast<size_t>(M) * 4 + 15) / 16 * 16 + 16;
+}
+
+int mica_w8a8_gemm_swiglu_quant(const int8_t* A, long lda, const int8_t* Bgu, long ldb, const float* sa,
+                                const float* sgu, const float* bias_gu, void* h_out, long ldh, int8_t* q_out, long ldq,
+                                float* s_out, int M, int I, int K, int round_mode, void* workspace,
+                                size_t workspace_bytes, void* stream) {
+    if (!A || !Bgu || !sa || !sgu || !h_out || !q_out || !s_out || (round_mode != 0 && round_mode != 1))
+        return MICA_ERR_ARG;
+    if (M < 0 || I < 16 || (I & 15) || K < 16 || (K & 15) || lda < K || ldb < K || ldh < I || ldq < I)
+        return MICA_ERR_SHAPE;
+    if (M > (1 << 30) || I > (1 << 29) || K > (1 << 30)) return MICA_ERR_RANGE;
+    if (!aligned16(A) || !aligned16(Bgu) || !aligned16(h_out) || !aligned16(q_out) || lda % 16 || ldb % 16 ||
+        (ldh * 2) % 16 || ldq % 16)
+        return MICA_ERR_ALIGN;
+    if (!workspace || !aligned16(workspace)) return workspace ? MICA_ERR_ALIGN : MICA_ERR_ARG;
+    if (workspace_bytes < mica_swiglu_workspace_bytes(M)) return MICA_ERR_WORKSPACE;
+    int sms = 0;
+    int rc = check_device(&sms);
+    if (rc) return rc;
+    if (M == 0) return MICA_OK;
+    const int N = 2 * I;
+    const long tiles256 = static_cast<long>((M + 127) / 128) * ((N + 255) / 256);
+    const int bn = tiles256 >= sms ? 256 : 128;
+    CUtensorMap ta, tb, th;
+    if ((rc = make_tmap_2d(&ta, A, CU_TENSOR_MAP_DATA_TYPE_UINT8, K, M, lda, 128, 128)) ||
+        (rc = make_tmap_2d(&tb, Bgu, CU_TENSOR_MAP_DATA_TYPE_UINT8, K, N, ldb, 128, bn)) ||
+        (rc = make_tmap_2d(&th, h_out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, I, M, ldh * 2, 64, 32)))
+        return rc;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    unsigned* amax = static_cast<unsigned*>(workspace);
+    unsigned* sync = reinterpret_cast<unsigned*>(static_cast<char*>(workspace) + (static_cast<size_t>(M) * 4 + 15) / 16 * 16);
+    cudaError_t e = cudaMemsetAsync(workspace, 0, mica_swiglu_workspace_bytes(M), st);
+    if (e != cudaSuccess) { set_cuda_error(e); return MICA_ERR_CUDA; }
+    GemmArgs g = {};
+    g.sa = sa; g.sb = sgu; g.bias = bias_gu; g.M = M; g.N = N; g.K = K; g.round_mode = round_mode;
+    g.row_amax = amax; g.grid_sync = sync;
+    g.h = static_cast<const __nv_bfloat16*>(h_out); g.ldh = ldh; g.q_out = q_out; g.ldq = ldq; g.s_out = s_out;
+    const long tiles = static_cast<long>((M + 127) / 128) * ((N + bn - 1) / bn);
+    const int grid = static_cast<int>(tiles < sms ? tiles : sms);
+    if (bn == 256) return gemm_launch<256, EPI_SWIGLU, __nv_bfloat16>(ta, tb, th, g, grid, true, st);
+    return gemm_launch<128, EPI_SWIGLU, __nv_bfloat16>(ta, tb, th, g, grid, true, st);
+}
+
+// ---------------------------------------------------------------------------------------
+int mica_option_logits(const void* h, int h_dtype, long ldh, const void* gamma, int norm_style, float eps,
+                       const float* rows, int n_rows, int D, const int* lo, const int* hi, float* logits, float* probs,
+                       int B, void* stream) {
+    if (!h || !rows || !logits || h_dtype < 0 || h_dtype > 2 ||
+        (norm_style != MICA_NORM_OFFSET && norm_style != MICA_NORM_WEIGHT))
+        return MICA_ERR_ARG;
+    if (gamma && h_dtype == MICA_DT_FP32) return MICA_ERR_UNSUPPORTED;
+    if (B < 0 || n_rows < 1 || n_rows > 4096 || D < 8 || (D & 7) || D > 4096 || ldh < D) return MICA_ERR_SHAPE;
+    const long es = static_cast<long>(dt_size(h_dtype));
+    if (!aligned16(h) || !aligned16(rows) || (gamma && !aligned16(gamma)) || (ldh * es) % 16) return MICA_ERR_ALIGN;
+    int rc = check_device(nullptr);
+    if (rc) return rc;
+    if (B == 0) return MICA_OK;
+    ReadoutArgs a = {};
+    a.h = h; a.ldh = ldh; a.gamma = gamma; a.norm_style = norm_style; a.eps = eps; a.rows = rows;
+    a.n_rows = n_rows; a.D = D; a.lo = lo; a.hi = hi; a.logits = logits; a.probs = probs; a.B = B;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const dim3 grid((n_rows + RO_WARPS - 1) / RO_WARPS), block(RO_WARPS * 32);
+    const size_t smem = static_cast<size_t>(D) * sizeof(float);
+#define RO_LAUNCH(T)                                                                                   \
+    do {                                                                                               \
+        if (D <= 1024) option_logits_kernel<T, 8><<<grid, block, smem, st>>>(a);                       \
+        else if (D <= 2048) option_logits_kernel<T, 16><<<grid, block, smem, st>>>(a);                 \
+        else if (D <= 2560) option_logits_kernel<T, 20><<<grid, block, smem, st>>>(a);                 \
+        else option_logits_kernel<T, 32><<<grid, block, smem, st>>>(a);                                \
+    } while (0)
+    if (h_dtype == MICA_DT_BF16) RO_LAUNCH(__nv_bfloat16);
+    else if (h_dtype == MICA_DT_FP16) RO_LAUNCH(__half);
+    else RO_LAUNCH(float);
+#undef RO_LAUNCH
+    if ((rc = launch_status())) return rc;
+    if (probs) {
+        option_softmax_kernel<<<(B + 7) / 8, 256, 0, st>>>(a);
+        return launch_status();
+    }
+    return MICA_OK;
+}
+
+// ---------------------------------------------------------------------------------------
+// Failure-detection self-test: one block waits on an mbarrier that never completes.
+__global__ void selftest_wait_kernel(int* status, unsigned long long limit_ns) {
+    __shared__ uint64_t bar;
+    __shared__ uint32_t abort_flag;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        abort_flag = 0;
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const bool ok = mbar_wait(&bar, 0, &abort_flag, MICA_DEV_TIMEOUT_SELFTEST, limit_ns);
+        *status = ok ? MICA_DEV_OK : MICA_DEV_TIMEOUT_SELFTEST;
+    }
+}
+
+int mica_selftest_wait_timeout(int* status_dev, int limit_us, void* stream) {
+    if (!status_dev || limit_us < 1 || limit_us > 2000000) return MICA_ERR_ARG;
+    int rc = check_device(nullptr);
+    if (rc) return rc;
+    selftest_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+        status_dev, static_cast<unsigned long long>(limit_us) * 1000ull);
+    return launch_status();
+}

@@ -1,0 +1,202 @@
+// quant.cuh -- per-token int8 activation quantiser and the fused RMSNorm + quantiser.
+//
+// One CTA per token row; each thread keeps up to QV vectors of 8 elements in registers,
+// so the row is read from HBM once (the reference kernel, v0.5/serving/kernel_src/
+// kernels.py:15-38, reads it twice: one pass for the absmax, one for the codes).
+// Memory-bound: per row 2K (bf16 in) + K (int8 out) + 4 bytes, plus y/sum when requested.
+#pragma once
+
+#include "common.cuh"
+
+namespace mica {
+
+constexpr int QV = 4;  // 8-element vectors cached per thread (K <= 1024 * 32)
+
+template <typename T>
+__device__ __forceinline__ void load8(const T* p, float (&f)[8]) {
+    if constexpr (sizeof(T) == 4) {
+        const float4 a = __ldg(reinterpret_cast<const float4*>(p));
+        const float4 b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+        f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
+        f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+    } else {
+        const uint4 v = __ldg(reinterpret_cast<const uint4*>(p));
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            if constexpr (std::is_same<T, __half>::value) {
+                const __half2 h = *reinterpret_cast<const __half2*>(&w[i]);
+                f[2 * i] = __low2float(h);
+                f[2 * i + 1] = __high2float(h);
+            } else {
+                f[2 * i] = __uint_as_float(w[i] << 16);
+                f[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+            }
+        }
+    }
+}
+
+template <typename T>
+__device__ __forceinline__ float round_to(float x) {
+    if constexpr (std::is_same<T, __half>::value) return __half2float(__float2half_rn(x));
+    else if constexpr (std::is_same<T, __nv_bfloat16>::value) return __bfloat162float(__float2bfloat16_rn(x));
+    else return x;
+}
+
+template <typename T>
+__device__ __forceinline__ void store8(T* p, const float (&f)[8]) {
+    if constexpr (sizeof(T) == 4) {
+        reinterpret_cast<float4*>(p)[0] = make_float4(f[0], f[1], f[2], f[3]);
+        reinterpret_cast<float4*>(p)[1] = make_float4(f[4], f[5], f[6], f[7]);
+    } else {
+        uint32_t w[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            if constexpr (std::is_same<T, __half>::value) {
+                __half2 h = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
+                w[i] = *reinterpret_cast<uint32_t*>(&h);
+            } else {
+                __nv_bfloat162 h = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+                w[i] = *reinterpret_cast<uint32_t*>(&h);
+            }
+        }
+        *reinterpret_cast<uint4*>(p) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+// Block-wide reduction; every thread gets the result. `red` holds 32 floats.
+template <bool MAX>
+__device__ __forceinline__ float block_reduce(float v, float* red) {
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    const int nw = (blockDim.x + 31) >> 5;
+    v = MAX ? warp_max(v) : warp_sum(v);
+    __syncthreads();                 // `red` may still be read from the previous reduction
+    if (l == 0) red[w] = v;
+    __syncthreads();
+    float r = l < nw ? red[l] : (MAX ? 0.f : 0.f);
+    r = MAX ? warp_max(r) : warp_sum(r);
+    return r;
+}
+
+struct QuantArgs {
+    const void* x; long ldx;
+    const void* residual; long ldr;
+    const void* gamma; int norm_style; float eps;
+    const float* inv;
+    void* y_out; long ldy;
+    void* sum_out; long ldsum;
+    int8_t* q; long ldq;
+    float* s;
+    int M, K, round_mode;
+};
+
+// NORM = false: mica_act_quant. NORM = true: mica_rmsnorm_quant.
+template <typename T, bool NORM>
+__global__ void __launch_bounds__(1024) quant_rows_kernel(const QuantArgs a) {
+    __shared__ float red[32];
+    const int row = blockIdx.x;
+    const int nvec = a.K >> 3;
+    const T* xr = static_cast<const T*>(a.x) + static_cast<long>(row) * a.ldx;
+    float v[QV][8];
+#pragma unroll
+    for (int i = 0; i < QV; ++i) {
+        const int idx = threadIdx.x + i * blockDim.x;
+        if (idx < nvec) {
+            load8(xr + idx * 8, v[i]);
+        } else {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) v[i][e] = 0.f;
+        }
+    }
+
+    if constexpr (NORM) {
+        if (a.residual != nullptr) {
+            const T* rr = static_cast<const T*>(a.residual) + static_cast<long>(row) * a.ldr;
+#pragma unroll
+            for (int i = 0; i < QV; ++i) {
+                const int idx = threadIdx.x + i * blockDim.x;
+                if (idx < nvec) {
+                    float r[8];
+                    load8(rr + idx * 8, r);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) v[i][e] = round_to<T>(__fadd_rn(v[i][e], r[e]));
+                    if (a.sum_out != nullptr)
+                        store8(static_cast<T*>(a.sum_out) + static_cast<long>(row) * a.ldsum + idx * 8, v[i]);
+                }
+            }
+        }
+        float ss = 0.f;
+#pragma unroll
+        for (int i = 0; i < QV; ++i)
+#pragma unroll
+            for (int e = 0; e < 8; ++e) ss = __fadd_rn(ss, __fmul_rn(v[i][e], v[i][e]));
+        ss = block_reduce<false>(ss, red);
+        const float rs = rsqrtf(__fadd_rn(__fdiv_rn(ss, static_cast<float>(a.K)), a.eps));
+        const T* gp = static_cast<const T*>(a.gamma);
+#pragma unroll
+        for (int i = 0; i < QV; ++i) {
+            const int idx = threadIdx.x + i * blockDim.x;
+            if (idx < nvec) {
+                float w[8];
+                load8(gp + idx * 8, w);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    const float n = __fmul_rn(v[i][e], rs);
+                    v[i][e] = a.norm_style == MICA_NORM_OFFSET ? round_to<T>(__fmul_rn(n, __fadd_rn(1.0f, w[e])))
+                                                               : round_to<T>(__fmul_rn(w[e], round_to<T>(n)));
+                }
+                if (a.y_out != nullptr)
+                    store8(static_cast<T*>(a.y_out) + static_cast<long>(row) * a.ldy + idx * 8, v[i]);
+            }
+        }
+    }
+
+    if (NORM && a.q == nullptr) return;  // norm-only call (fused_kernels.rms_norm drop-in)
+    if (a.inv != nullptr) {
+#pragma unroll
+        for (int i = 0; i < QV; ++i) {
+            const int idx = threadIdx.x + i * blockDim.x;
+            if (idx < nvec) {
+                const float4 i0 = __ldg(reinterpret_cast<const float4*>(a.inv + idx * 8));
+                const float4 i1 = __ldg(reinterpret_cast<const float4*>(a.inv + idx * 8) + 1);
+                const float iv[8] = {i0.x, i0.y, i0.z, i0.w, i1.x, i1.y, i1.z, i1.w};
+#pragma unroll
+                for (int e = 0; e < 8; ++e) v[i][e] = __fmul_rn(v[i][e], iv[e]);
+            }
+        }
+    }
+    float am = 0.f;
+#pragma unroll
+    for (int i = 0; i < QV; ++i)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) am = fmaxf(am, fabsf(v[i][e]));
+    am = block_reduce<true>(am, red);
+    const float scale = __fdiv_rn(fmaxf(am, 1e-8f), 127.0f);
+    int8_t* qr = a.q + static_cast<long>(row) * a.ldq;
+#pragma unroll
+    for (int i = 0; i < QV; ++i) {
+        const int idx = threadIdx.x + i * blockDim.x;
+        if (idx < nvec) {
+            uint32_t o[2] = {0u, 0u};
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const int qv = quant_round(__fdiv_rn(v[i][e], scale), a.round_mode);
+                o[e >> 2] |= (static_cast<uint32_t>(qv) & 0xFFu) << ((e & 3) * 8);
+            }
+            *reinterpret_cast<uint2*>(qr + idx * 8) = make_uint2(o[0], o[1]);
+        }
+    }
+    if (threadIdx.x == 0) a.s[row] = scale;
+}
+
+}  // namespace mica

@@ -1,0 +1,280 @@
+"""Drop-in for the reference's quantised-module surface, v0.5/serving/lib/int8_runtime.py.
+
+QLinear keeps the reference's buffers and attributes (qweight int8 [N,K], wscale fp32 [N],
+inv_smooth fp32 [K] | None, bias fp32 [N] | None, w16, in_features, out_features, out_dtype,
+backend, mode; :108-192) so weights converted or loaded for the reference load here
+unchanged. forward() runs two kernels -- per-token quantiser and W8A8 GEMM -- through
+int8_kernels (:172-192).
+
+Differences, by design:
+  * backend 'aot' only. A kernel miss raises KernelMiss (the reference silently falls back
+    to torch ops; set FALLBACK['allowed'] = True to get that behaviour, on the GPU).
+  * FusedMLP replaces gate_proj / up_proj / act / down_proj with the fused gate_up GEMM
+    (SwiGLU + requantisation in its epilogue) and the down GEMM: 2 kernels instead of the
+    reference's 2 quantisers + 3 GEMMs + SwiGLU (lib/fast_runtime.py:126-132).
+"""
+from __future__ import annotations
+
+import torch
+from torch import nn
+
+from . import int8_kernels as aot
+
+ALPHA = 0.5
+EPS = 1e-08
+PRECISION = {'mode': 'int8'}
+FALLBACK = {'allowed': False}
+GDN = ('in_proj_qkv', 'in_proj_z', 'in_proj_a', 'in_proj_b', 'out_proj')
+ATTN = ('q_proj', 'k_proj', 'v_proj', 'o_proj')
+MLP = ('gate_proj', 'up_proj', 'down_proj')
+GROUPS = {'gdn': GDN, 'attn': ATTN, 'mlp': MLP, 'ffn': MLP, 'all': GDN + ATTN + MLP}
+
+
+class KernelMiss(RuntimeError):
+    """The W8A8 kernels could not serve a call (reason as in int8_kernels.STATS['fallback'])."""
+
+
+def quant_weight(w: torch.Tensor):
+    """Per-output-row int8 weights, the reference's int8_quant.quant_weight (lib/int8_quant.py:54-62)."""
+    wf = w.float()
+    s = wf.abs().amax(1).clamp_min(EPS) / 127.0
+    q = torch.round(wf / s[:, None]).clamp(-127, 127).to(torch.int8)
+    return q, s
+
+
+def smooth_factors(act_amax, w, alpha=ALPHA, lo=1e-4, hi=1e4):
+    """SmoothQuant factors, the reference's int8_quant.smooth_factors (lib/int8_quant.py:80-86)."""
+    a = act_amax.float().to(w.device)
+    wmax = w.float().abs().amax(0)
+    s = a.clamp_min(EPS).pow(alpha) / wmax.clamp_min(EPS).pow(1.0 - alpha)
+    s = torch.where((a > 0) & (wmax > 0), s, torch.ones_like(s))
+    return s.clamp(lo, hi)
+
+
+def _last_miss(before):
+    now = aot.STATS['fallback']
+    return ', '.join(f'{k}+{v - before.get(k, 0)}' for k, v in now.items() if v != before.get(k, 0)) or 'unknown'
+
+
+def _torch_fallback(x2, inv, qweight, wscale, bias, out_dtype):
+    """The reference's own fallback (int8_quant.quant_act + torch._int_mm + dequant,
+    lib/int8_runtime.py:181-192), on the GPU; only reached with FALLBACK['allowed']."""
+    xf = x2.float() * inv if inv is not None else x2.float()
+    s = xf.abs().amax(-1).clamp_min(EPS) / 127.0
+    q = torch.round(xf / s[:, None]).clamp(-127, 127).to(torch.int8)
+    m = q.shape[0]
+    qp = torch.cat((q, q.new_zeros(32 - m, q.shape[1])), 0) if m <= 16 else q
+    y = torch._int_mm(qp, qweight.t())[:m].float() * s[:, None] * wscale[None, :]
+    return (y + bias if bias is not None else y).to(out_dtype)
+
+
+class QLinear(nn.Module):
+    def __init__(self, linear, smooth=None, backend='aot', keep_bf16=False):
+        super().__init__()
+        if backend != 'aot':
+            raise ValueError("mica_b200 QLinear serves backend='aot' only (the CPU emulation is the test oracle)")
+        w = linear.weight.detach()
+        self.register_buffer('w16', w.contiguous() if keep_bf16 else None)
+        self.in_features, self.out_features = (w.shape[1], w.shape[0])
+        self.out_dtype, self.backend, self.mode = (w.dtype, backend, 'int8')
+        wf = w.float()
+        if smooth is not None:
+            smooth = smooth.float().to(w.device)
+            wf = wf * smooth[None, :]
+            self.register_buffer('inv_smooth', (1.0 / smooth).contiguous())
+        else:
+            self.inv_smooth = None
+        q, s = quant_weight(wf)
+        self.register_buffer('qweight', q.contiguous())
+        self.register_buffer('wscale', s.contiguous())
+        self.register_buffer('bias', None if linear.bias is None else linear.bias.detach().float().contiguous())
+
+    @classmethod
+    def empty(cls, in_features, out_features, out_dtype=torch.bfloat16, backend='aot', smooth=True, bias=False):
+        """Shape-only module for file loading (reference :130-144)."""
+        self = cls.__new__(cls)
+        nn.Module.__init__(self)
+        self.register_buffer('w16', None)
+        self.in_features, self.out_features = (in_features, out_features)
+        self.out_dtype, self.backend, self.mode = (out_dtype, backend, 'int8')
+        meta = lambda *shape, dtype=torch.float32: torch.empty(*shape, dtype=dtype, device='meta')  # noqa: E731
+        if smooth:
+            self.register_buffer('inv_smooth', meta(in_features))
+        else:
+            self.inv_smooth = None
+        self.register_buffer('qweight', meta(out_features, in_features, dtype=torch.int8))
+        self.register_buffer('wscale', meta(out_features))
+        self.register_buffer('bias', meta(out_features) if bias else None)
+        return self
+
+    @property
+    def weight(self):
+        w = self.qweight.float() * self.wscale.reshape(-1, 1)
+        return (w * self.inv_smooth[None, :] if self.inv_smooth is not None else w).to(self.out_dtype)
+
+    def _quant(self, x2):
+        before = dict(aot.STATS['fallback'])
+        r = aot.act_quant(x2.contiguous(), self.inv_smooth)
+        if r is None and not FALLBACK['allowed']:
+            raise KernelMiss(f'act_quant miss ({_last_miss(before)}) for x {tuple(x2.shape)} {x2.dtype}')
+        return r
+
+    def rows_forward(self, x, ranges):
+        """One quantisation, several GEMMs over row ranges of the weight (reference :153-170)."""
+        if self.w16 is not None and PRECISION['mode'] == 'bf16':
+            return None
+        shape = x.shape
+        x2 = x.reshape(-1, shape[-1])
+        r = self._quant(x2)
+        outs = []
+        for lo, hi in ranges:
+            w, s = (self.qweight[lo:hi], self.wscale[lo:hi])
+            b = None if self.bias is None else self.bias[lo:hi]
+            y = None
+            if r is not None:
+                before = dict(aot.STATS['fallback'])
+                y = aot.mm_i8(r[0], r[1], w, s, b, self.out_dtype)
+                if y is None and not FALLBACK['allowed']:
+                    raise KernelMiss(f'mm_i8 miss ({_last_miss(before)}) for rows {lo}:{hi}')
+            if y is None:
+                y = _torch_fallback(x2, self.inv_smooth, w, s, b, self.out_dtype)
+            outs.append(y.reshape(*shape[:-1], hi - lo))
+        return outs
+
+    def forward(self, x):
+        if self.w16 is not None and PRECISION['mode'] == 'bf16':
+            return nn.functional.linear(x, self.w16, None if self.bias is None else self.bias.to(self.w16.dtype))
+        shape = x.shape
+        x2 = x.reshape(-1, shape[-1])
+        if x2.shape[0] == 0:
+            return x.new_zeros(*shape[:-1], self.out_features, dtype=self.out_dtype)
+        r = self._quant(x2)
+        y = None
+        if r is not None:
+            before = dict(aot.STATS['fallback'])
+            y = aot.mm_i8(r[0], r[1], self.qweight, self.wscale, self.bias, self.out_dtype)
+            if y is None and not FALLBACK['allowed']:
+                raise KernelMiss(f'mm_i8 miss ({_last_miss(before)}) for N {self.out_features} K {self.in_features}')
+        if y is None:
+            y = _torch_fallback(x2, self.inv_smooth, self.qweight, self.wscale, self.bias, self.out_dtype)
+        return y.reshape(*shape[:-1], self.out_features)
+
+
+def interleave_gate_up(gate: torch.Tensor, up: torch.Tensor, group: int = 16) -> torch.Tensor:
+    """Fused gate_up row order: `group` gate rows, then the same `group` up rows, repeated
+    (what the SwiGLU epilogue of mica_w8a8_gemm_swiglu_quant expects). [I, ...] -> [2I, ...]."""
+    i = gate.shape[0]
+    if i % group or up.shape != gate.shape:
+        raise ValueError(f'gate/up shapes {tuple(gate.shape)} {tuple(up.shape)} not interleavable by {group}')
+    g = gate.reshape(i // group, group, *gate.shape[1:])
+    u = up.reshape(i // group, group, *up.shape[1:])
+    return torch.cat([g, u], dim=1).reshape(2 * i, *gate.shape[1:]).contiguous()
+
+
+class FusedMLP(nn.Module):
+    """SwiGLU MLP as two kernels: [gate|up] GEMM + SwiGLU + requant, then the down GEMM.
+
+    Built from a module with gate_proj / up_proj / down_proj Linears (HF Qwen3MLP) or from
+    existing QLinears. Smoothing vectors must be absent or shared by gate and up (one
+    quantisation of x feeds both); down_proj's own smoothing is not supported here
+    because its input is quantised inside the gate_up kernel."""
+
+    def __init__(self, mlp, stats=None, prefix='', alpha=ALPHA):
+        super().__init__()
+        g, u, d = mlp.gate_proj, mlp.up_proj, mlp.down_proj
+        get = (lambda name: stats.get(prefix + name)) if stats is not None else (lambda name: None)
+        if isinstance(g, QLinear):
+            qg, sg, qu, su, inv = g.qweight, g.wscale, u.qweight, u.wscale, g.inv_smooth
+            if (g.inv_smooth is None) != (u.inv_smooth is None) or (
+                    g.inv_smooth is not None and not torch.equal(g.inv_smooth, u.inv_smooth)):
+                raise ValueError('gate_proj and up_proj need the same smoothing to share one quantisation')
+            bg, bu = g.bias, u.bias
+            self.down = d if isinstance(d, QLinear) else QLinear(d)
+            self.out_dtype = g.out_dtype
+        else:
+            amax = get('gate_proj')
+            smooth = None
+            if amax is not None:
+                smooth = smooth_factors(amax, torch.cat([g.weight.detach(), u.weight.detach()]), alpha)
+            wg, wu = g.weight.detach().float(), u.weight.detach().float()
+            if smooth is not None:
+                smooth = smooth.float().to(wg.device)
+                wg, wu = wg * smooth[None, :], wu * smooth[None, :]
+            qg, sg = quant_weight(wg)
+            qu, su = quant_weight(wu)
+            inv = None if smooth is None else (1.0 / smooth).contiguous()
+            bg = None if g.bias is None else g.bias.detach().float()
+            bu = None if u.bias is None else u.bias.detach().float()
+            self.down = QLinear(d)
+            self.out_dtype = g.weight.dtype
+        if self.down.inv_smooth is not None:
+            raise ValueError('down_proj smoothing is not supported by the fused MLP')
+        self.inner = qg.shape[0]
+        self.register_buffer('inv_smooth', inv)
+        self.register_buffer('qweight_gu', interleave_gate_up(qg, qu))
+        self.register_buffer('wscale_gu', interleave_gate_up(sg, su))
+        self.register_buffer('bias_gu', None if bg is None and bu is None else interleave_gate_up(
+            bg if bg is not None else torch.zeros_like(bu), bu if bu is not None else torch.zeros_like(bg)))
+
+    def quantise_input(self, x2):
+        before = dict(aot.STATS['fallback'])
+        r = aot.act_quant(x2.contiguous(), self.inv_smooth)
+        if r is None:
+            raise KernelMiss(f'act_quant miss ({_last_miss(before)})')
+        return r
+
+    def forward_quantised(self, qx, sx):
+        before = dict(aot.STATS['fallback'])
+        r = aot.mm_i8_swiglu_quant(qx, sx, self.qweight_gu, self.wscale_gu, self.bias_gu)
+        if r is None:
+            raise KernelMiss(f'gate_up miss ({_last_miss(before)})')
+        _, qh, sh = r
+        y = aot.mm_i8(qh, sh, self.down.qweight, self.down.wscale, self.down.bias, self.out_dtype)
+        if y is None:
+            raise KernelMiss(f'down_proj miss ({_last_miss(before)})')
+        return y
+
+    def forward(self, x):
+        shape = x.shape
+        x2 = x.reshape(-1, shape[-1])
+        if x2.shape[0] == 0:
+            return x.new_zeros(*shape[:-1], self.down.out_features, dtype=self.out_dtype)
+        qx, sx = self.quantise_input(x2)
+        return self.forward_quantised(qx, sx).reshape(*shape[:-1], self.down.out_features)
+
+
+def target_linears(body, layers=None, modules=None):
+    """(qualified name, parent, attr, Linear) for every projection in `body.layers`
+    (reference lib/int8_quant.py:99-110)."""
+    names = GROUPS['all'] if modules is None else tuple(modules)
+    wanted = range(len(body.layers)) if layers is None else layers
+    out = []
+    for i in wanted:
+        layer = body.layers[i]
+        for path, parent in layer.named_modules():
+            for attr, child in parent.named_children():
+                if attr in names and isinstance(child, nn.Linear):
+                    out.append((f'layers.{i}.{path + "." if path else ""}{attr}', parent, attr, child))
+    return out
+
+
+def convert(body, stats, backend='aot', alpha=ALPHA, keep_bf16=False, fuse_mlp=False):
+    """Replace every projection Linear with QLinear (reference :195-206). With fuse_mlp,
+    each `mlp` that has gate/up/down projections becomes a FusedMLP instead.
+    Returns (replaced, smoothed)."""
+    replaced = smoothed = 0
+    if fuse_mlp:
+        for i, layer in enumerate(body.layers):
+            mlp = getattr(layer, 'mlp', None)
+            if mlp is not None and all(isinstance(getattr(mlp, n, None), nn.Linear) for n in MLP):
+                layer.mlp = FusedMLP(mlp, stats, f'layers.{i}.mlp.', alpha)
+                replaced += 3
+                smoothed += layer.mlp.inv_smooth is not None
+    for qname, parent, attr, child in target_linears(body):
+        amax = stats.get(qname) if stats is not None else None
+        smooth = None if amax is None else smooth_factors(amax, child.weight.detach(), alpha)
+        setattr(parent, attr, QLinear(child, smooth, backend, keep_bf16=keep_bf16))
+        replaced += 1
+        smoothed += smooth is not None
+        del child
+    return (replaced, smoothed)

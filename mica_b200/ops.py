@@ -1,0 +1,163 @@
+"""PyTorch custom ops over the libmica_w8a8 C ABI.
+
+Each op allocates its outputs with torch (so CUDA-graph capture draws them from the
+graph's pool, as the reference's torch.empty outputs do, v0.5/serving/lib/
+int8_kernels.py:343-344, :376) and launches on torch's current stream of the input's
+device (:261-265). Fake (meta) implementations let torch.compile and graph tooling see
+shapes without running anything.
+
+    torch.ops.mica.act_quant(x, inv, round_mode)                       -> (q, s)
+    torch.ops.mica.rmsnorm_quant(x, residual, gamma, inv, eps, style, round_mode, want_y)
+                                                                        -> (q, s, y, sum)
+    torch.ops.mica.w8a8_gemm(qx, sx, qw, sw, bias, out_dtype, block_n)  -> y
+    torch.ops.mica.gemm_swiglu_quant(qx, sx, qw_gu, sw_gu, bias, round_mode) -> (h, q, s)
+    torch.ops.mica.option_logits(h, rows, gamma, lo, hi, eps, style)    -> (logits, probs)
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from . import _native as N
+
+DTYPE_CODE = {torch.bfloat16: N.DT_BF16, torch.float16: N.DT_FP16, torch.float32: N.DT_FP32}
+OUT_DTYPES = {0: torch.bfloat16, 1: torch.float16, 2: torch.float32}
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+class _on:
+    """Makes the tensor's device current for the C side (cudaGetDevice)."""
+
+    def __init__(self, t: torch.Tensor):
+        self.idx = t.device.index
+
+    def __enter__(self):
+        self.prev = torch.cuda.current_device()
+        if self.prev != self.idx:
+            torch.cuda.set_device(self.idx)
+
+    def __exit__(self, *exc):
+        if self.prev != self.idx:
+            torch.cuda.set_device(self.prev)
+
+
+# ---------------------------------------------------------------------------------------
+@torch.library.custom_op('mica::act_quant', mutates_args=())
+def act_quant(x: torch.Tensor, inv: Optional[torch.Tensor], round_mode: int) -> tuple[torch.Tensor, torch.Tensor]:
+    m, k = x.shape
+    q = torch.empty((m, k), dtype=torch.int8, device=x.device)
+    s = torch.empty((m,), dtype=torch.float32, device=x.device)
+    with _on(x):
+        N.call('mica_act_quant', x.data_ptr(), DTYPE_CODE[x.dtype], x.stride(0), _ptr(inv), q.data_ptr(), q.stride(0),
+               s.data_ptr(), m, k, round_mode, _stream(x))
+    return q, s
+
+
+@act_quant.register_fake
+def _(x, inv, round_mode):
+    m, k = x.shape
+    return x.new_empty((m, k), dtype=torch.int8), x.new_empty((m,), dtype=torch.float32)
+
+
+# ---------------------------------------------------------------------------------------
+@torch.library.custom_op('mica::rmsnorm_quant', mutates_args=())
+def rmsnorm_quant(x: torch.Tensor, residual: Optional[torch.Tensor], gamma: torch.Tensor, inv: Optional[torch.Tensor],
+                  eps: float, style: int, round_mode: int, want_y: bool, want_q: bool
+                  ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    m, k = x.shape
+    dev = x.device
+    q = torch.empty((m, k) if want_q else (0,), dtype=torch.int8, device=dev)
+    s = torch.empty((m,) if want_q else (0,), dtype=torch.float32, device=dev)
+    y = torch.empty((m, k) if want_y else (0,), dtype=x.dtype, device=dev)
+    sm = torch.empty((m, k) if residual is not None else (0,), dtype=x.dtype, device=dev)
+    with _on(x):
+        N.call('mica_rmsnorm_quant', x.data_ptr(), DTYPE_CODE[x.dtype], x.stride(0),
+               _ptr(residual), residual.stride(0) if residual is not None else 0,
+               gamma.data_ptr(), style, eps, _ptr(inv),
+               y.data_ptr() if want_y else None, k if want_y else 0,
+               sm.data_ptr() if residual is not None else None, k if residual is not None else 0,
+               q.data_ptr() if want_q else None, k if want_q else 0, s.data_ptr() if want_q else None,
+               m, k, round_mode, _stream(x))
+    return q, s, y, sm
+
+
+@rmsnorm_quant.register_fake
+def _(x, residual, gamma, inv, eps, style, round_mode, want_y, want_q):
+    m, k = x.shape
+    return (x.new_empty((m, k) if want_q else (0,), dtype=torch.int8),
+            x.new_empty((m,) if want_q else (0,), dtype=torch.float32),
+            x.new_empty((m, k) if want_y else (0,)),
+            x.new_empty((m, k) if residual is not None else (0,)))
+
+
+# ---------------------------------------------------------------------------------------
+@torch.library.custom_op('mica::w8a8_gemm', mutates_args=())
+def w8a8_gemm(qx: torch.Tensor, sx: torch.Tensor, qw: torch.Tensor, sw: torch.Tensor, bias: Optional[torch.Tensor],
+              out_dtype: int, block_n: int) -> torch.Tensor:
+    m, k = qx.shape
+    n = qw.shape[0]
+    out = torch.empty((m, n), dtype=OUT_DTYPES[out_dtype], device=qx.device)
+    with _on(qx):
+        N.call('mica_w8a8_gemm_cfg', qx.data_ptr(), qx.stride(0), qw.data_ptr(), qw.stride(0), sx.data_ptr(),
+               sw.data_ptr(), _ptr(bias), out.data_ptr(), out_dtype, out.stride(0), m, n, k, block_n, 0, _stream(qx))
+    return out
+
+
+@w8a8_gemm.register_fake
+def _(qx, sx, qw, sw, bias, out_dtype, block_n):
+    return qx.new_empty((qx.shape[0], qw.shape[0]), dtype=OUT_DTYPES[out_dtype])
+
+
+# ---------------------------------------------------------------------------------------
+@torch.library.custom_op('mica::gemm_swiglu_quant', mutates_args=())
+def gemm_swiglu_quant(qx: torch.Tensor, sx: torch.Tensor, qw_gu: torch.Tensor, sw_gu: torch.Tensor,
+                      bias: Optional[torch.Tensor], round_mode: int
+                      ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    m, k = qx.shape
+    i = qw_gu.shape[0] // 2
+    dev = qx.device
+    h = torch.empty((m, i), dtype=torch.bfloat16, device=dev)
+    q = torch.empty((m, i), dtype=torch.int8, device=dev)
+    s = torch.empty((m,), dtype=torch.float32, device=dev)
+    ws_bytes = N.lib().mica_swiglu_workspace_bytes(m)
+    ws = torch.empty((max(ws_bytes, 16),), dtype=torch.uint8, device=dev)
+    with _on(qx):
+        N.call('mica_w8a8_gemm_swiglu_quant', qx.data_ptr(), qx.stride(0), qw_gu.data_ptr(), qw_gu.stride(0),
+               sx.data_ptr(), sw_gu.data_ptr(), _ptr(bias), h.data_ptr(), h.stride(0), q.data_ptr(), q.stride(0),
+               s.data_ptr(), m, i, k, round_mode, ws.data_ptr(), ws.numel(), _stream(qx))
+    return h, q, s
+
+
+@gemm_swiglu_quant.register_fake
+def _(qx, sx, qw_gu, sw_gu, bias, round_mode):
+    m, i = qx.shape[0], qw_gu.shape[0] // 2
+    return (qx.new_empty((m, i), dtype=torch.bfloat16), qx.new_empty((m, i), dtype=torch.int8),
+            qx.new_empty((m,), dtype=torch.float32))
+
+
+# ---------------------------------------------------------------------------------------
+@torch.library.custom_op('mica::option_logits', mutates_args=())
+def option_logits(h: torch.Tensor, rows: torch.Tensor, gamma: Optional[torch.Tensor], lo: Optional[torch.Tensor],
+                  hi: Optional[torch.Tensor], eps: float, style: int) -> tuple[torch.Tensor, torch.Tensor]:
+    b, d = h.shape
+    r = rows.shape[0]
+    logits = torch.empty((b, r), dtype=torch.float32, device=h.device)
+    probs = torch.empty((b, r), dtype=torch.float32, device=h.device)
+    with _on(h):
+        N.call('mica_option_logits', h.data_ptr(), DTYPE_CODE[h.dtype], h.stride(0), _ptr(gamma), style, eps,
+               rows.data_ptr(), r, d, _ptr(lo), _ptr(hi), logits.data_ptr(), probs.data_ptr(), b, _stream(h))
+    return logits, probs
+
+
+@option_logits.register_fake
+def _(h, rows, gamma, lo, hi, eps, style):
+    b, r = h.shape[0], rows.shape[0]
+    return h.new_empty((b, r), dtype=torch.float32), h.new_empty((b, r), dtype=torch.float32)

@@ -1,0 +1,110 @@
+"""GEMM tile table: the `--kernel-tune pinned|full` mechanism for the W8A8 GEMM.
+
+The reference pins one Triton specialisation per (N, K, bias, dtype, M%16, M-class) in
+v0.5/serving/kernel_src/specs/sm100.json, picked at launch by the M-class table
+GEMM_CLASSES (v0.5/serving/lib/int8_kernels.py:356, :381-385); its FLA autotune caches are
+pinned or re-tuned on the device and persisted in --state-dir (lib/kernel_state.py:111-256,
+lib/release_runtime.py:1260-1333).
+
+Here a key is (N, K, M-class) and the value the GEMM's output-tile width block_n
+(64 / 128 / 256; 0 = let the library choose). `pinned` ships with the package
+(tiles_sm100a.json); `full` sweeps block_n on the device for the shapes in use and writes
+the winners to <state_dir>/tiles_sm100a.json, which later runs load first.
+"""
+from __future__ import annotations
+
+import json
+import os
+import threading
+from pathlib import Path
+
+HERE = Path(__file__).resolve().parent
+PINNED = HERE / 'tiles_sm100a.json'
+STATE_NAME = 'tiles_sm100a.json'
+CLASSES = ((128, 's'), (384, 'm'), (1024, 'n'))
+CHOICES = (64, 128, 256)
+
+_TABLE = None
+_LOCK = threading.Lock()
+_STATE = {'dir': os.environ.get('MICA_STATE_DIR')}
+
+
+def m_class(m: int) -> str:
+    return next((c for hi, c in CLASSES if m <= hi), 'l')
+
+
+def key(n: int, k: int, m: int) -> str:
+    return f'mm|N{n}|K{k}|c{m_class(m)}'
+
+
+def _load(path: Path) -> dict:
+    try:
+        data = json.loads(path.read_text(encoding='utf-8'))
+    except (OSError, ValueError):
+        return {}
+    entries = data.get('entries', {}) if isinstance(data, dict) else {}
+    return {k: int(v) for k, v in entries.items() if int(v) in (0,) + CHOICES}
+
+
+def table() -> dict:
+    global _TABLE
+    if _TABLE is None:
+        with _LOCK:
+            if _TABLE is None:
+                t = _load(PINNED)
+                if _STATE['dir']:
+                    t.update(_load(Path(_STATE['dir']) / STATE_NAME))
+                _TABLE = t
+    return _TABLE
+
+
+def set_state_dir(path) -> None:
+    """Use <path>/tiles_sm100a.json (tuned entries) on top of the pinned table."""
+    global _TABLE
+    with _LOCK:
+        _STATE['dir'] = str(path) if path else None
+        _TABLE = None
+
+
+def block_n(n: int, k: int, m: int) -> int:
+    return table().get(key(n, k, m), 0)
+
+
+def tune(shapes, device='cuda', reps: int = 20, state_dir=None) -> dict:
+    """Sweeps block_n for each (N, K, M) on the device; returns {key: best} and, with a
+    state dir, persists it there. Times with CUDA events on the current stream."""
+    import torch
+
+    from . import ops
+
+    out = {}
+    dev = torch.device(device)
+    for n, k, m in shapes:
+        g = torch.Generator(device=dev).manual_seed(n * 7 + k * 13 + m)
+        qx = torch.randint(-127, 128, (m, k), generator=g, device=dev, dtype=torch.int8)
+        qw = torch.randint(-127, 128, (n, k), generator=g, device=dev, dtype=torch.int8)
+        sx = torch.rand(m, generator=g, device=dev) * 1e-2 + 1e-3
+        sw = torch.rand(n, generator=g, device=dev) * 1e-2 + 1e-3
+        best, best_t = 0, float('inf')
+        for bn in CHOICES:
+            for _ in range(3):
+                torch.ops.mica.w8a8_gemm(qx, sx, qw, sw, None, 0, bn)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            for _ in range(reps):
+                torch.ops.mica.w8a8_gemm(qx, sx, qw, sw, None, 0, bn)
+            b.record()
+            b.synchronize()
+            t = a.elapsed_time(b) / reps
+            if t < best_t:
+                best, best_t = bn, t
+        out[key(n, k, m)] = best
+    if state_dir:
+        p = Path(state_dir)
+        p.mkdir(parents=True, exist_ok=True)
+        old = _load(p / STATE_NAME)
+        old.update(out)
+        (p / STATE_NAME).write_text(json.dumps({'format': 'mica-tiles/1', 'entries': old}, indent=1, sort_keys=True))
+        set_state_dir(p)
+    del ops
+    return out

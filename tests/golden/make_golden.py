@@ -1,0 +1,209 @@
+"""Generates tests/golden/*.npz by running the REFERENCE's own code on seeded inputs.
+
+Run in the build container, where the reference checkout is available (it is read, never
+copied; only inputs/outputs are saved):
+
+    python tests/golden/make_golden.py [/path/to/reference]
+
+What runs (all on CPU):
+  * the reference's Triton kernels v0.5/serving/kernel_src/kernels.py act_quant and mm_i8,
+    and lib/fused_kernels.py norm / swiglu, under Triton's CPU interpreter
+    (TRITON_INTERPRET=1). The interpreter's fp32 -> bf16 cast truncates, so the Triton
+    kernels write fp32 outputs here and the cast is applied afterwards (RNE, as on GPU);
+  * the reference's torch path: int8_quant.quant_act / quant_weight / int_gemm_exact,
+    int8_runtime.QLinear(..., backend='emulate'), fused_kernels.rms_norm / swi_glu CPU
+    branches, and the readout of release_runtime.py:302-306 restated on a
+    Qwen3RMSNorm + gathered lm_head rows.
+"""
+from __future__ import annotations
+
+import os
+import sys
+import types
+from pathlib import Path
+
+os.environ['TRITON_INTERPRET'] = '1'
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+HERE = Path(__file__).resolve().parent
+REF = Path(sys.argv[1] if len(sys.argv) > 1 else '/root/reference')
+sys.path.insert(0, str(REF / 'v0.5' / 'serving' / 'lib'))
+sys.path.insert(0, str(REF / 'v0.5' / 'serving' / 'kernel_src'))
+
+import fused_kernels as fk  # noqa: E402
+import int8_quant as wq  # noqa: E402
+import int8_runtime as rt  # noqa: E402
+import kernels as ksrc  # noqa: E402
+
+torch.set_num_threads(8)
+
+
+def bits(t: torch.Tensor) -> np.ndarray:
+    assert t.dtype == torch.bfloat16
+    return t.contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def triton_act_quant(x, inv):
+    m, k = x.shape
+    q = torch.empty((m, k), dtype=torch.int8)
+    s = torch.empty((m,), dtype=torch.float32)
+    ksrc.act_quant[(m,)](x, inv if inv is not None else s, q, s, k, x.stride(0), q.stride(0),
+                         HAS_INV=inv is not None, BLOCK=1024)
+    return q, s
+
+
+def triton_mm_i8_f32(qx, qw, sx, sw, bias):
+    m, k = qx.shape
+    n = qw.shape[0]
+    c = torch.empty((m, n), dtype=torch.float32)
+    bm, bn = 16, 64
+    grid = ((m + bm - 1) // bm) * ((n + bn - 1) // bn)
+    ksrc.mm_i8[(grid,)](qx, qw, sx, sw, bias if bias is not None else sw, c, m, n, k, qx.stride(0), 1, qw.stride(0), 1,
+                        c.stride(0), 1, HAS_BIAS=bias is not None, BM=bm, BN=bn, BK=128, GROUP_M=8)
+    return c
+
+
+def act_cases(g):
+    out = {}
+    for name, (m, k, smooth, outl) in {
+        'a': (3, 2560, False, False),
+        'b': (17, 4096, True, False),
+        'c': (48, 2560, False, True),
+        'd': (5, 9728, True, True),
+        'e': (2, 64, False, False),
+        'f': (4, 256, False, False),
+    }.items():
+        x = torch.randn(m, k, generator=g)
+        if outl:
+            ch = torch.randperm(k, generator=g)[:8]
+            x[:, ch] *= 50
+        x = x.to(torch.bfloat16)
+        inv = (torch.rand(k, generator=g) * 2 + 0.1).float() if smooth else None
+        if name == 'f':
+            # tie-rich: absmax 127/8 gives scale exactly 1/8, so x = n/16 quantises to n/2
+            x = (torch.round(torch.randn(m, k, generator=g) * 8) / 16).to(torch.bfloat16)
+            x[:, 0] = 127 / 8
+        q_away, s_away = triton_act_quant(x, inv)
+        q_even, s_even = wq.quant_act(x, inv, 'int8')
+        out[name] = dict(x=bits(x), inv=np.zeros(0, np.float32) if inv is None else inv.numpy(),
+                         q_away=q_away.numpy(), s_away=s_away.numpy(), q_even=q_even.numpy(), s_even=s_even.numpy())
+    return out
+
+
+def gemm_cases(g):
+    out = {}
+    for name, (m, n, k, has_bias) in {
+        'a': (7, 64, 2560, False),
+        'b': (33, 32, 4096, True),
+        'c': (130, 48, 512, False),
+        'd': (1, 32, 9728, True),
+    }.items():
+        x = torch.randn(m, k, generator=g).to(torch.bfloat16)
+        w = (torch.randn(n, k, generator=g) * 0.05).to(torch.bfloat16)
+        bias = (torch.randn(n, generator=g) * 0.1).to(torch.bfloat16) if has_bias else None
+        lin = types.SimpleNamespace(weight=w, bias=bias)
+        ql = rt.QLinear(lin, None, 'emulate')
+        y_ref = ql(x)                                   # the reference's own QLinear (torch path)
+        qx, sx = wq.quant_act(x, None, 'int8')
+        acc = wq.int_gemm_exact(qx, ql.qweight)
+        acc2 = wq.torch_int_mm(qx, ql.qweight)
+        assert torch.equal(acc, acc2)
+        y32 = triton_mm_i8_f32(qx, ql.qweight, sx, ql.wscale, ql.bias)  # the reference Triton kernel
+        out[name] = dict(x=bits(x), bias=np.zeros(0, np.float32) if bias is None else ql.bias.numpy(),
+                         qw=ql.qweight.numpy(), sw=ql.wscale.numpy(), qx=qx.numpy(), sx=sx.numpy(), acc=acc.numpy(),
+                         y_triton_f32=y32.numpy(), y_qlinear=bits(y_ref))
+    return out
+
+
+@torch.no_grad()
+def norm_cases(g):
+    _, norm_k, swiglu_k = fk._kernels()
+    out = {}
+    for name, (m, k, with_res) in {'a': (4, 2560, False), 'b': (9, 2560, True), 'c': (3, 1024, True)}.items():
+        x = torch.randn(m, k, generator=g).to(torch.bfloat16)
+        r = torch.randn(m, k, generator=g).to(torch.bfloat16) if with_res else None
+        w = (torch.randn(k, generator=g) * 0.1).to(torch.bfloat16)   # (1 + w) convention
+        eps = 1e-6
+        res = fk.rms_norm(x, w, eps, r)                       # reference CPU branch
+        y_cpu, s_cpu = (res if r is not None else (res, x))
+        # reference Triton kernel, fp32 outputs
+        y32 = torch.empty((m, k), dtype=torch.float32)
+        s32 = torch.empty((m, k), dtype=torch.float32)
+        xin = x
+        norm_k[(m,)](xin, y32, w, r if r is not None else xin, s32, k, xin.stride(0),
+                     (r if r is not None else xin).stride(0), eps, r is not None, 1 << (k - 1).bit_length())
+        # HF Qwen3RMSNorm with a gamma ~ N(1, 0.1) weight
+        from transformers.models.qwen3.modeling_qwen3 import Qwen3RMSNorm
+        hf = Qwen3RMSNorm(k, eps=eps)
+        gam = (1 + 0.1 * torch.randn(k, generator=g)).to(torch.bfloat16)
+        hf.weight.data = gam.clone()
+        hf = hf.to(torch.bfloat16)
+        src = s_cpu if r is not None else x
+        y_hf = hf(src)
+        out[name] = dict(x=bits(x), r=np.zeros(0, np.uint16) if r is None else bits(r), w=bits(w), eps=np.float32(eps),
+                         y_cpu=bits(y_cpu), sum_cpu=bits(s_cpu), y_triton_f32=y32.numpy(), gamma=bits(gam),
+                         y_hf=bits(y_hf))
+    # swiglu
+    gt = (torch.randn(6, 1024, generator=g) * 3).to(torch.bfloat16)
+    ut = torch.randn(6, 1024, generator=g).to(torch.bfloat16)
+    y_cpu = fk.swi_glu(gt, ut)
+    y32 = torch.empty((6, 1024), dtype=torch.float32)
+    swiglu_k[(6,)](gt, ut, y32, gt.numel())
+    out['swiglu'] = dict(g=bits(gt), u=bits(ut), y_cpu=bits(y_cpu), y_triton_f32=y32.numpy())
+    return out
+
+
+@torch.no_grad()
+def readout_cases(g):
+    from transformers.models.qwen3.modeling_qwen3 import Qwen3RMSNorm
+    d, vocab, b = 256, 1000, 3
+    lm = (torch.randn(vocab, d, generator=g) * 0.05).to(torch.bfloat16)
+    ids = torch.randperm(vocab, generator=g)[:40]
+    weight = lm.index_select(0, ids).float().clone()      # release_runtime.py:302
+    norm = Qwen3RMSNorm(d, eps=1e-6)
+    norm.weight.data = (1 + 0.1 * torch.randn(d, generator=g)).to(torch.bfloat16)
+    norm = norm.to(torch.bfloat16)
+    h = torch.randn(b, d, generator=g).to(torch.bfloat16)
+    hn = norm(h)
+    z = torch.nn.functional.linear(hn.float(), weight).float()   # release_runtime.py:304-306
+    lo = np.array([0, 2, 2], np.int32)
+    hi = np.array([2, 40, 9], np.int32)
+    probs = np.zeros((b, weight.shape[0]), np.float32)
+    for i in range(b):
+        probs[i, lo[i]:hi[i]] = z[i, lo[i]:hi[i]].softmax(-1).numpy()   # release_runtime.py:509-522
+    return {'a': dict(h=bits(h), gamma=bits(norm.weight.data), rows=weight.numpy(), hn=bits(hn), logits=z.numpy(),
+                      lo=lo, hi=hi, probs=probs)}
+
+
+@torch.no_grad()
+def selftest_cases(g):
+    """Inputs shaped like the reference's start-up self-test (int8_runtime.py:362-443)."""
+    gs = torch.Generator().manual_seed(rt.SELFTEST_SEED)
+    n, k = 32, 2560
+    w = (torch.randn(n, k, generator=gs) * 0.05).to(torch.bfloat16)
+    amax = torch.rand(k, generator=gs) * 4 + 0.05
+    amax[::61] *= 25.0
+    smooth = wq.smooth_factors(amax, w, rt.ALPHA)
+    lin = types.SimpleNamespace(weight=w, bias=None)
+    q = rt.QLinear(lin, smooth, 'emulate')
+    x = (torch.randn(24, k, generator=gs) * amax / 3).to(torch.bfloat16)
+    y = q(x)
+    return {'a': dict(amax=amax.numpy(), smooth=smooth.numpy(), inv=q.inv_smooth.numpy(),
+                      qw=q.qweight.numpy(), sw=q.wscale.numpy(), x=bits(x), y=bits(y))}
+
+
+def save(name, cases):
+    flat = {f'{c}/{k}': v for c, d in cases.items() for k, v in d.items()}
+    np.savez_compressed(HERE / f'{name}.npz', **flat)
+    print(name, sum(v.nbytes for v in flat.values()) // 1024, 'KiB raw')
+
+
+if __name__ == '__main__':
+    g = torch.Generator().manual_seed(20261201)
+    save('act_quant', act_cases(g))
+    save('gemm', gemm_cases(g))
+    save('norm', norm_cases(g))
+    save('readout', readout_cases(g))
+    save('selftest', selftest_cases(g))
