@@ -1,0 +1,419 @@
+"""Benchmark of the W8A8 linear-layer hot path (BASELINE metric: W8A8 GEMM TOPS).
+
+Workload: the four projections of one decoder layer of the 4B model,
+QKV 2560->6144, O 4096->2560, gate_up 2560->19456, down 9728->2560, each a full W8A8
+linear (per-token int8 quantiser + tcgen05 GEMM with dequant epilogue -> bf16), at
+M in {256, 2048, 8192, 32768} tokens. One step = the whole sweep (16 linears,
+43264 * 201.85 MOP = 8.733 TOP of GEMM work). Synthetic seeded data: activations bf16
+N(0,1), int8 weights uniform in [-127, 127], per-channel scales uniform in [1e-3, 1e-2].
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mica|reference]
+
+value  : GEMM TOPS of the sweep, inputs resident in HBM, one CUDA-graph replay per step
+         timed with CUDA events (L2 flushed between steps by a 256 MiB write outside
+         the timed events); whole-job = N x per-rank ops / max-over-ranks time.
+e2e    : the same sweep through the public API (QLinear-style calls) from pinned HOST
+         buffers, the H2D copy of every input and D2H copy of every output inside the
+         timed region.
+roofline: the GEMM kernel alone (per-launch CUDA events, averaged over the sweep's
+         shapes) against 2 x the measured bf16 dense peak (B200 dense int8 = 2 x bf16).
+--impl reference: the reference's CPU path (the oracle's restatement of int8_quant
+         quant_act + int_gemm_exact + dequant, numpy/float64 BLAS on all host threads) on a
+         bounded sample: the four projections at M=256 per step.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+PROJECTIONS = (('qkv', 6144, 2560), ('o', 2560, 4096), ('gate_up', 19456, 2560), ('down', 2560, 9728))
+MS = (256, 2048, 8192, 32768)
+OPS_PER_TOKEN = sum(2 * n * k for _, n, k in PROJECTIONS)   # 201.85 MOP per token per layer
+METRIC = 'W8A8 GEMM TOPS'
+UNIT = 'TOPS'
+CONFIG = {'workload': 'config1: 4B decoder-layer projection sweep (QKV/O/gate_up/down) x M{256,2048,8192,32768}',
+          'model': 'Qwen3-4B-shaped dense layer (hidden 2560, 32q/8kv x 128, FFN 9728), random int8 weights',
+          'tokens_per_step': sum(MS), 'gemm_ops_per_step': OPS_PER_TOKEN * sum(MS), 'l2': 'flushed (256 MiB write) between steps',
+          'parallelism': 'data-parallel replicas, no collective'}
+
+
+def load_oracle():
+    import importlib.util
+    spec = importlib.util.spec_from_file_location('mica_oracle', ROOT / 'oracle' / 'mica_oracle.py')
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def peaks():
+    p = ROOT / 'MEASURED_PEAKS.json'
+    if p.is_file():
+        d = json.loads(p.read_text())
+        return {'bf16': float(d['bf16_tflops']), 'hbm': float(d['hbm_gbs']), 'source': 'measured'}
+    return {'bf16': 1590.0, 'hbm': 6650.0, 'source': 'fallback'}
+
+
+# ---------------------------------------------------------------------------------------
+def cpu_sample(O, rows=256, reps=1, seed=0):
+    """The reference's CPU path on a bounded sample: quantise + exact int GEMM + dequant
+    for the four projections at `rows` tokens. Returns (ops, seconds)."""
+    import numpy as np
+    rng = np.random.default_rng(seed)
+    data = []
+    for _, n, k in PROJECTIONS:
+        x = O.round_bf16(rng.standard_normal((rows, k), dtype=np.float32))
+        qw = rng.integers(-127, 128, (n, k), dtype=np.int8)
+        sw = rng.uniform(1e-3, 1e-2, n).astype(np.float32)
+        data.append((x, qw, sw))
+    ops = 0
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        for x, qw, sw in data:
+            qx, sx = O.quant_act_half_even(x)
+            O.dequant_out(O.int_gemm_exact(qx, qw), sx, sw)
+            ops += 2 * rows * qw.shape[0] * qw.shape[1]
+    return ops, time.perf_counter() - t0
+
+
+def cpu_threads():
+    try:
+        import threadpoolctl
+        info = threadpoolctl.threadpool_info()
+        blas = [i['num_threads'] for i in info if i.get('user_api') == 'blas']
+        if blas:
+            return max(blas)
+    except Exception:
+        pass
+    return os.cpu_count() or 1
+
+
+# ---------------------------------------------------------------------------------------
+class Clocks:
+    """Samples SM clock and throttle reasons with nvidia-smi during the timed region."""
+    Q = ('index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,'
+         'clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,'
+         'clocks_event_reasons.sw_power_cap')
+
+    def __init__(self, index):
+        self.index, self.proc, self.lines = index, None, []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(['nvidia-smi', '-i', str(self.index), f'--query-gpu={self.Q}',
+                                          '--format=csv,noheader,nounits', '-lms', '100'],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except (OSError, ValueError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ('hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap')
+        for line in self.lines:
+            f = [x.strip() for x in line.split(',')]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for name, v in zip(names, f[5:9]):
+                if v.lower().startswith('active'):
+                    reasons.add(name)
+        return {'sm_mhz': statistics.median(sm) if sm else None, 'sm_max_mhz': mx, 'reasons': sorted(reasons),
+                'samples': len(sm)}
+
+
+# ---------------------------------------------------------------------------------------
+def run_mica(args, rank, world, local):
+    import torch
+    import mica_b200.int8_kernels as K
+    from mica_b200 import _native as Nat
+
+    dev = torch.device('cuda', local)
+    torch.cuda.set_device(dev)
+    ok, why = K.available(dev)
+    if not ok:
+        raise SystemExit(f'mica kernels unavailable: {why}')
+    K.preload(dev)
+    g = torch.Generator(device=dev).manual_seed(1234 + rank)
+    weights = {}
+    for name, n, k in PROJECTIONS:
+        weights[name] = (torch.randint(-127, 128, (n, k), generator=g, device=dev, dtype=torch.int8),
+                         torch.rand(n, generator=g, device=dev) * 9e-3 + 1e-3)
+    xs = {}
+    for m in MS:
+        for k in sorted({k for _, _, k in PROJECTIONS}):
+            xs[m, k] = torch.randn(m, k, generator=g, device=dev).to(torch.bfloat16)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def step():
+        outs = []
+        for m in MS:
+            for name, n, k in PROJECTIONS:
+                q, s = torch.ops.mica.act_quant(xs[m, k], None, 0)
+                outs.append(torch.ops.mica.w8a8_gemm(q, s, weights[name][0], weights[name][1], None, 0, 0))
+        return outs
+
+    launches_per_step = 2 * len(MS) * len(PROJECTIONS)
+    # ---- capture the sweep into one CUDA graph ----
+    s = torch.cuda.Stream(device=dev)
+    s.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(s):
+        for _ in range(2):
+            step()
+    torch.cuda.current_stream(dev).wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        static_out = step()
+    torch.cuda.synchronize(dev)
+    del static_out
+
+    def timed(fn, steps, warmup):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            torch.distributed.barrier()
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        for a, b in ev:
+            flush.fill_(1)                      # evict L2 between steps (outside the events)
+            a.record()
+            fn()
+            b.record()
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            torch.distributed.barrier()
+        return sum(a.elapsed_time(b) for a, b in ev)   # ms
+
+    try:
+        gpu_id = 'GPU-' + str(torch.cuda.get_device_properties(dev).uuid)   # physical GPU, whatever the remap
+    except Exception:
+        gpu_id = str(local)
+    with Clocks(gpu_id) as clk:
+        # keep the GPU busy until the sampler reports (bounded), then time
+        t0 = time.time()
+        while len(clk.lines) < 2 and time.time() - t0 < 3.0:
+            graph.replay()
+            torch.cuda.synchronize(dev)
+        ms_total = timed(graph.replay, args.steps, args.warmup)
+        time.sleep(0.25)
+    clocks = clk.summary()
+
+    # ---- per-GEMM kernel timing for the roofline: event-record nodes inside a CUDA graph
+    # bracket each GEMM launch exactly (an eager launch would also time Python's launch
+    # latency); L2 is flushed before every bracketed launch. ----
+    gemm_ms, gemm_ops, reps = 0.0, 0, 5
+    for m in MS:
+        for name, n, k in PROJECTIONS:
+            q, sc = torch.ops.mica.act_quant(xs[m, k], None, 0)
+            w, sw = weights[name]
+            for _ in range(3):
+                torch.ops.mica.w8a8_gemm(q, sc, w, sw, None, 0, 0)
+            ev = [(torch.cuda.Event(enable_timing=True, external=True),
+                   torch.cuda.Event(enable_timing=True, external=True)) for _ in range(reps)]
+            g2 = torch.cuda.CUDAGraph()
+            s2 = torch.cuda.Stream(device=dev)
+            s2.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(s2):
+                torch.ops.mica.w8a8_gemm(q, sc, w, sw, None, 0, 0)
+            torch.cuda.current_stream(dev).wait_stream(s2)
+            with torch.cuda.graph(g2):
+                for a, b in ev:
+                    flush.fill_(1)
+                    a.record()
+                    torch.ops.mica.w8a8_gemm(q, sc, w, sw, None, 0, 0)
+                    b.record()
+            g2.replay()
+            g2.replay()
+            torch.cuda.synchronize(dev)
+            gemm_ms += sum(a.elapsed_time(b) for a, b in ev) / reps
+            gemm_ops += 2 * m * n * k
+            del g2
+
+    # ---- e2e: host buffers through the public API, copies inside the timed region ----
+    host_x = {key: t.cpu().pin_memory() for key, t in xs.items()}
+    host_y = {}
+    for m in MS:
+        for name, n, k in PROJECTIONS:
+            host_y[m, name] = torch.empty((m, n), dtype=torch.bfloat16).pin_memory()
+    h2d = sum(host_x[m, k].numel() * 2 for m in MS for _, _, k in PROJECTIONS)
+    d2h = sum(t.numel() * 2 for t in host_y.values())
+
+    def e2e_step():
+        for m in MS:
+            for name, n, k in PROJECTIONS:
+                x = host_x[m, k].to(dev, non_blocking=True)
+                q, sc = K.act_quant(x, None)
+                y = K.mm_i8(q, sc, weights[name][0], weights[name][1], None, torch.bfloat16)
+                host_y[m, name].copy_(y, non_blocking=True)
+
+    e2e_steps = max(1, min(args.steps, 5))
+    e2e_ms = timed(e2e_step, e2e_steps, 1)
+
+    import torch.distributed as dist
+    t = torch.tensor([ms_total, e2e_ms, gemm_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_total, e2e_ms, gemm_ms = t.tolist()
+    if rank != 0:
+        return None
+    step_ops = OPS_PER_TOKEN * sum(MS)
+    ms_step = ms_total / args.steps
+    value = world * step_ops * args.steps / (ms_total * 1e-3) / 1e12
+    e2e_value = world * step_ops * e2e_steps / (e2e_ms * 1e-3) / 1e12
+    pk = peaks()
+    peak_int8 = 2 * pk['bf16']
+    achieved = gemm_ops / (gemm_ms * 1e-3) / 1e12
+    traffic = None
+    prof = ROOT / 'profiles' / 'gemm_i8_traffic.json'
+    if prof.is_file():
+        try:
+            traffic = json.loads(prof.read_text()).get('traffic_bytes_per_launch_avg')
+        except ValueError:
+            traffic = None
+    line = {
+        'metric': METRIC, 'value': round(value, 2), 'unit': UNIT, 'n_gpus': world, 'steps': args.steps,
+        'warmup': args.warmup, 'ms_per_step': round(ms_step, 4), 'higher_is_better': True, 'scaling': 'weak',
+        'vs_baseline': None, 'dtype': 'int8 x int8 -> int32 (bf16 out)', 'data': 'synthetic (seeded)',
+        'config': CONFIG,
+        'e2e': {'value': round(e2e_value, 2), 'unit': UNIT, 'h2d_bytes_per_step': h2d, 'd2h_bytes_per_step': d2h},
+        'gpu_launches': launches_per_step * args.steps,
+        'roofline': {'bound': 'tensor', 'achieved': round(achieved, 1), 'peak': round(peak_int8, 1),
+                     'unit': 'TOPS (int8)', 'frac': round(achieved / peak_int8, 4), 'traffic': traffic,
+                     'peak_source': f"2 x {pk['source']} bf16 dense ({pk['bf16']} TFLOP/s); nominal dense int8 4500",
+                     'frac_of_nominal_4500': round(achieved / 4500.0, 4)},
+        'clocks': clocks,
+    }
+    return line
+
+
+def run_cpu_baseline(seconds=10.0):
+    O = load_oracle()
+    cpu_sample(O, rows=32)  # warm
+    ops, secs, reps = 0, 0.0, 0
+    while secs < seconds and reps < 50:
+        o, s = cpu_sample(O, rows=256, seed=reps)
+        ops += o
+        secs += s
+        reps += 1
+    return {'value': round(ops / secs / 1e12, 4), 'unit': UNIT, 'cores': cpu_threads(), 'kind': 'port',
+            'sample': f'{reps} x (4 projections at M=256: quantise + exact int GEMM + dequant), {secs:.1f} s'}
+
+
+def run_reference(args):
+    O = load_oracle()
+    cpu_sample(O, rows=32)
+    for i in range(args.warmup):
+        cpu_sample(O, rows=256, seed=100 + i)
+    ops, secs = 0, 0.0
+    for i in range(args.steps):
+        o, s = cpu_sample(O, rows=256, seed=i)
+        ops += o
+        secs += s
+    v = ops / secs / 1e12
+    cores = cpu_threads()
+    return {
+        'impl': 'reference', 'metric': METRIC, 'value': round(v, 4), 'unit': UNIT, 'n_gpus': args.gpus,
+        'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': round(secs / args.steps * 1e3, 2),
+        'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None, 'dtype': 'int8 x int8 -> int32 (fp64 BLAS)',
+        'data': 'synthetic (seeded)', 'config': CONFIG,
+        'cpu_baseline': {'value': round(v, 4), 'unit': UNIT, 'cores': cores, 'kind': 'port',
+                         'sample': 'per step: the 4 projections at M=256 (quantise + exact int GEMM + dequant)'},
+        'e2e': {'value': round(v, 4), 'unit': UNIT, 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0},
+    }
+
+
+def run_shape(args):
+    """One W8A8 linear shape (quantiser + GEMM), for profiler captures: prints ms and TOPS."""
+    import torch
+    import mica_b200.int8_kernels as K
+    m, n, k = (int(v) for v in args.shape.split(','))
+    dev = torch.device('cuda', 0)
+    K.preload(dev)
+    g = torch.Generator(device=dev).manual_seed(7)
+    x = torch.randn(m, k, generator=g, device=dev).to(torch.bfloat16)
+    w = torch.randint(-127, 128, (n, k), generator=g, device=dev, dtype=torch.int8)
+    sw = torch.rand(n, generator=g, device=dev) * 9e-3 + 1e-3
+    q, s = torch.ops.mica.act_quant(x, None, 0)
+    for _ in range(args.warmup):
+        torch.ops.mica.w8a8_gemm(q, s, w, sw, None, 0, args.block_n)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.steps):
+        q, s = torch.ops.mica.act_quant(x, None, 0)
+        torch.ops.mica.w8a8_gemm(q, s, w, sw, None, 0, args.block_n)
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / args.steps
+    print(json.dumps({'shape': [m, n, k], 'block_n': args.block_n, 'ms_per_linear': round(ms, 4),
+                      'tops_incl_quant': round(2 * m * n * k / ms / 1e9, 1)}), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument('--gpus', type=int, default=1)
+    ap.add_argument('--steps', type=int, default=100)
+    ap.add_argument('--warmup', type=int, default=5)
+    ap.add_argument('--impl', choices=('mica', 'reference'), default='mica')
+    ap.add_argument('--cpu-seconds', type=float, default=10.0)
+    ap.add_argument('--shape', default=None, help='M,N,K: time one linear shape only (profiling)')
+    ap.add_argument('--block-n', type=int, default=0)
+    args = ap.parse_args()
+    if args.shape:
+        run_shape(args)
+        return
+    if args.warmup < 3:
+        ap.error('--warmup must be >= 3')
+    rank = int(os.environ.get('RANK', 0))
+    world = int(os.environ.get('WORLD_SIZE', 1))
+    local = int(os.environ.get('LOCAL_RANK', 0))
+    if args.impl == 'reference':
+        if rank == 0:
+            print(json.dumps(run_reference(args)), flush=True)
+        return
+    if world > 1:
+        import datetime
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=120), device_id=torch.device('cuda', local))
+    try:
+        line = run_mica(args, rank, world, local)
+        if rank == 0:
+            line['cpu_baseline'] = run_cpu_baseline(args.cpu_seconds)
+            print(json.dumps(line), flush=True)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+            dist.destroy_process_group()
+
+
+if __name__ == '__main__':
+    main()

@@ -141,7 +141,7 @@ __global__ void __launch_bounds__(1024) quant_rows_kernel(const QuantArgs a) {
 #pragma unroll
             for (int e = 0; e < 8; ++e) ss = __fadd_rn(ss, __fmul_rn(v[i][e], v[i][e]));
         ss = block_reduce<false>(ss, red);
-        const float rs = rsqrtf(__fadd_rn(__fdiv_rn(ss, static_cast<float>(a.K)), a.eps));
+        const float rs = __frsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(a.K)), a.eps));
         const T* gp = static_cast<const T*>(a.gamma);
 #pragma unroll
         for (int i = 0; i < QV; ++i) {

@@ -56,7 +56,7 @@ __global__ void __launch_bounds__(RO_WARPS * 32) option_logits_kernel(const Read
         float rs = 1.f;
         if (a.gamma != nullptr) {
             ss = block_reduce<false>(ss, red);
-            rs = rsqrtf(__fadd_rn(__fdiv_rn(ss, static_cast<float>(D)), a.eps));
+            rs = __frsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(D)), a.eps));
         }
         __syncthreads();  // previous request's dot products are done with hn
         for (int idx = threadIdx.x; idx < nvec; idx += blockDim.x) {

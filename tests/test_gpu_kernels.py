@@ -196,8 +196,11 @@ def test_rmsnorm_quant_outliers(K, m):
     q, s, y, _ = K.rmsnorm_quant(x.cuda(), gam.cuda(), 1e-6, None, style=1, want_y=True)
     yo, _ = O.rms_norm(x.float().numpy(), gam.float().numpy(), 1e-6, None, style='weight')
     yk = to_np(y)
+    # HF style rounds twice (normalised value, then times gamma): a 1-ulp difference in
+    # the first rounding can become 2 ulp after the second (still < 1e-2 relative)
     ulp = np.abs(O.f32_to_bf16_bits(yk).astype(int) - O.f32_to_bf16_bits(yo).astype(int))
-    assert ulp.max() <= 1
+    assert ulp.max() <= 2 and (ulp > 0).mean() < 0.01
+    assert np.allclose(yk, yo, rtol=1e-2, atol=0)
     q2, s2 = O.quant_act_half_away(yk)
     assert np.array_equal(q.cpu().numpy(), q2) and np.array_equal(s.cpu().numpy(), s2)
 

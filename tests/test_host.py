@@ -1,0 +1,138 @@
+"""Host-side logic that needs no GPU: the reference-facing surface's miss contract, weight
+conversion, gate/up interleave, tile table, and the failure paths."""
+import numpy as np
+import pytest
+import torch
+
+from conftest import ORACLE as O
+
+
+def test_available_reports_no_cuda_here_or_sm100_there():
+    import mica_b200.int8_kernels as K
+    ok, why = K.available()
+    if not torch.cuda.is_available():
+        assert not ok and 'CUDA' in why
+    else:
+        assert isinstance(ok, bool)
+
+
+def test_misses_return_none_and_count_reasons_like_the_reference():
+    import mica_b200.int8_kernels as K
+    before = dict(K.STATS['fallback'])
+    assert K.act_quant(torch.zeros(4, 64)) is None                      # CPU tensor
+    assert K.mm_i8(torch.zeros(4, 64), torch.ones(4), torch.zeros(8, 64, dtype=torch.int8), torch.ones(8)) is None
+    assert K.attn_fwd(None, None, None, 1.0) is None
+    after = K.STATS['fallback']
+    assert after['act_input'] == before.get('act_input', 0) + 1
+    assert after['mm_input'] == before.get('mm_input', 0) + 1
+    assert after['no_cubin'] == before.get('no_cubin', 0) + 1
+    assert K.attn_keys() == []
+
+
+def test_qlinear_weight_conversion_matches_reference_quant_weight():
+    from mica_b200.int8_runtime import QLinear
+    g = torch.Generator().manual_seed(0)
+    lin = torch.nn.Linear(256, 48, bias=True)
+    lin.weight.data = (torch.randn(48, 256, generator=g) * 0.05).to(torch.bfloat16)
+    lin.bias.data = torch.randn(48, generator=g).to(torch.bfloat16)
+    q = QLinear(lin)
+    qo, so = O.quant_weight(lin.weight.detach().float().numpy())
+    assert np.array_equal(q.qweight.numpy(), qo) and np.array_equal(q.wscale.numpy(), so)
+    assert q.bias.dtype == torch.float32 and q.inv_smooth is None
+    assert q.out_dtype == torch.bfloat16 and q.in_features == 256 and q.out_features == 48
+    w = q.weight
+    assert w.shape == (48, 256) and w.dtype == torch.bfloat16
+
+
+def test_qlinear_smoothing_folds_into_weights():
+    from mica_b200.int8_runtime import QLinear, smooth_factors
+    g = torch.Generator().manual_seed(1)
+    lin = torch.nn.Linear(128, 32, bias=False)
+    lin.weight.data = torch.randn(32, 128, generator=g) * 0.05
+    amax = torch.rand(128, generator=g) * 4 + 0.05
+    sm = smooth_factors(amax, lin.weight.detach())
+    smo = O.smooth_factors(amax.numpy(), lin.weight.detach().numpy())
+    assert np.allclose(sm.numpy(), smo, rtol=1e-6)
+    q = QLinear(lin, sm)
+    assert torch.allclose(q.inv_smooth * sm, torch.ones(128), rtol=1e-6)
+
+
+def test_qlinear_empty_has_meta_buffers():
+    from mica_b200.int8_runtime import QLinear
+    q = QLinear.empty(2560, 9728, smooth=True, bias=False)
+    assert q.qweight.device.type == 'meta' and q.qweight.shape == (9728, 2560) and q.inv_smooth.shape == (2560,)
+
+
+def test_qlinear_rejects_emulate_backend():
+    from mica_b200.int8_runtime import QLinear
+    with pytest.raises(ValueError):
+        QLinear(torch.nn.Linear(16, 16), backend='emulate')
+
+
+def test_qlinear_forward_raises_loudly_without_the_gpu_path():
+    from mica_b200.int8_runtime import KernelMiss, QLinear
+    q = QLinear(torch.nn.Linear(64, 32))
+    with pytest.raises(KernelMiss):
+        q(torch.randn(3, 64).to(torch.bfloat16))
+
+
+def test_interleave_gate_up_matches_oracle_layout():
+    from mica_b200.int8_runtime import interleave_gate_up
+    g = torch.arange(64 * 5).reshape(64, 5)
+    u = -g
+    assert np.array_equal(interleave_gate_up(g, u).numpy(), O.interleave_gate_up(g.numpy(), u.numpy()))
+    s = torch.arange(64.0)
+    assert np.array_equal(interleave_gate_up(s, -s).numpy(), O.interleave_gate_up(s.numpy(), -s.numpy()))
+    with pytest.raises(ValueError):
+        interleave_gate_up(torch.zeros(24, 3), torch.zeros(24, 3))
+
+
+def test_fused_mlp_builds_from_hf_qwen3_mlp():
+    from transformers import Qwen3Config
+    from transformers.models.qwen3.modeling_qwen3 import Qwen3MLP
+
+    from mica_b200.int8_runtime import FusedMLP
+    cfg = Qwen3Config(hidden_size=128, intermediate_size=256)
+    mlp = Qwen3MLP(cfg)
+    f = FusedMLP(mlp)
+    assert f.qweight_gu.shape == (512, 128) and f.wscale_gu.shape == (512,)
+    assert f.down.qweight.shape == (128, 256)
+    # the first 16 rows are gate rows, the next 16 up rows
+    qg, _ = O.quant_weight(mlp.gate_proj.weight.detach().numpy())
+    qu, _ = O.quant_weight(mlp.up_proj.weight.detach().numpy())
+    assert np.array_equal(f.qweight_gu[:16].numpy(), qg[:16]) and np.array_equal(f.qweight_gu[16:32].numpy(), qu[:16])
+
+
+def test_convert_replaces_every_projection():
+    from transformers import Qwen3Config
+    from transformers.models.qwen3.modeling_qwen3 import Qwen3Model
+
+    from mica_b200.int8_runtime import FusedMLP, QLinear, convert
+    cfg = Qwen3Config(hidden_size=64, intermediate_size=128, num_hidden_layers=2, num_attention_heads=4,
+                      num_key_value_heads=2, head_dim=16, vocab_size=100)
+    body = Qwen3Model(cfg)
+    n, sm = convert(body, None)
+    assert (n, sm) == (14, 0)
+    assert isinstance(body.layers[0].self_attn.q_proj, QLinear)
+    body2 = Qwen3Model(cfg)
+    n, _ = convert(body2, None, fuse_mlp=True)
+    assert n == 14 and isinstance(body2.layers[1].mlp, FusedMLP)
+
+
+def test_tile_table_keys_use_reference_m_classes(tmp_path):
+    from mica_b200 import tiles
+    assert [tiles.m_class(m) for m in (1, 128, 129, 384, 385, 1024, 1025)] == ['s', 's', 'm', 'm', 'n', 'n', 'l']
+    assert tiles.key(6144, 2560, 4096) == 'mm|N6144|K2560|cl'
+    (tmp_path / tiles.STATE_NAME).write_text('{"format": "mica-tiles/1", "entries": {"mm|N64|K64|cs": 128}}')
+    tiles.set_state_dir(tmp_path)
+    try:
+        assert tiles.block_n(64, 64, 7) == 128
+        assert tiles.block_n(64, 64, 700) == 0
+    finally:
+        tiles.set_state_dir(None)
+
+
+def test_native_errors_name_the_status():
+    from mica_b200 import _native as N
+    with pytest.raises(N.NativeError, match='ERR_SHAPE'):
+        N.check('mica_x', 2)
