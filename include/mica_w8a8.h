@@ -169,6 +169,32 @@ int mica_w8a8_gemm_swiglu_quant(const int8_t* A, long lda, const int8_t* Bgu, lo
                                 int M, int I, int K, int round_mode,
                                 void* workspace, size_t workspace_bytes, void* stream);
 
+/* The same fused gate_up + SwiGLU + requantisation, for callers that cannot allocate
+ * device memory. No counterpart in the reference.
+ * Who needs it: a host that has already handed all of the GPU's memory to its own
+ * planner (a serving runtime that sizes its context cap against the whole device), or a
+ * plugin whose host owns the allocator and forbids cudaMalloc on the serving path because
+ * an allocation there can block or fail in the middle of a request. Such callers cannot
+ * supply the workspace that mica_w8a8_gemm_swiglu_quant needs.
+ * Instead, this entry point uses a scratch array compiled into the library
+ * (MICA_NOALLOC_SCRATCH_BYTES per GPU that loads it, held until the process exits). It
+ * calls no cudaMalloc, cudaFree or other allocating routine. The caller still passes every
+ * input and output.
+ * Limit: M <= MICA_NOALLOC_MAX_ROWS; larger M returns MICA_ERR_WORKSPACE before any work.
+ * Set-up: the first call on each device looks up the scratch array's device address,
+ * with that device current. Make that first call before any stream capture (a warm-up
+ * call is enough).
+ * Sharing: every call on a device uses the same scratch, and each call clears what must
+ * start at zero. Calls whose kernels overlap on the GPU (other streams, other threads)
+ * race on that scratch: serialise them.                                                   */
+#define MICA_NOALLOC_MAX_ROWS       65536
+#define MICA_NOALLOC_SCRATCH_BYTES  (65536 * 4 + 16)
+int mica_w8a8_gemm_swiglu_quant_noalloc(const int8_t* A, long lda, const int8_t* Bgu, long ldb,
+                                        const float* sa, const float* sgu, const float* bias_gu,
+                                        void* h_out, long ldh,
+                                        int8_t* q_out, long ldq, float* s_out,
+                                        int M, int I, int K, int round_mode, void* stream);
+
 /* Option-logit scorer for the last position of each request:
  *   hn[b]       = optional RMSNorm of h[b] (gamma NULL = h used as given; gamma has
  *                 h's dtype, norm_style MICA_NORM_*)

@@ -74,6 +74,10 @@ SIGNATURES = {
         _I,
         [_P, _L, _P, _L, _P, _P, _P, _P, _L, _P, _L, _P, _I, _I, _I, _I, _P, _Z, _P],
     ),
+    'mica_w8a8_gemm_swiglu_quant_noalloc': (
+        _I,
+        [_P, _L, _P, _L, _P, _P, _P, _P, _L, _P, _L, _P, _I, _I, _I, _I, _P],
+    ),
     'mica_option_logits': (_I, [_P, _I, _L, _P, _I, _F, _P, _I, _I, _P, _P, _P, _P, _I, _P]),
     'mica_selftest_wait_timeout': (_I, [_P, _I, _P]),
 }

@@ -393,6 +393,56 @@ int mica_w8a8_gemm_swiglu_quant(const int8_t* A, long lda, const int8_t* Bgu, lo
 }
 
 // ---------------------------------------------------------------------------------------
+// Allocation-free variant of the fused SwiGLU chain, for callers that cannot call
+// cudaMalloc (see include/mica_w8a8.h). Its scratch -- one row-max word per token plus the
+// grid-barrier counter, laid out exactly as the workspace of mica_w8a8_gemm_swiglu_quant --
+// is this file-scope device array. Each GPU that loads the library holds one copy until
+// the process exits.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[MICA_NOALLOC_SCRATCH_BYTES];
+static_assert(MICA_NOALLOC_SCRATCH_BYTES >= (static_cast<size_t>(MICA_NOALLOC_MAX_ROWS) * 4 + 15) / 16 * 16 + 16,
+              "scratch must hold the workspace of MICA_NOALLOC_MAX_ROWS rows");
+
+// Device address of g_noalloc_scratch per device. In host code the array's name is only a
+// host-side stand-in, so the address is looked up once per device (with that device
+// current) and cached; the lookup itself allocates nothing.
+static void* g_noalloc_addr[kMaxDev] = {};
+static std::mutex g_noalloc_lock;
+
+static int noalloc_scratch(void** out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) { set_cuda_error(e); return MICA_ERR_CUDA; }
+    if (dev < 0 || dev >= kMaxDev) return MICA_ERR_ARCH;
+    std::lock_guard<std::mutex> g(g_noalloc_lock);
+    if (g_noalloc_addr[dev] == nullptr) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess || p == nullptr) {
+            set_cuda_error(e != cudaSuccess ? e : cudaErrorInvalidSymbol);
+            return MICA_ERR_CUDA;
+        }
+        g_noalloc_addr[dev] = p;
+    }
+    *out = g_noalloc_addr[dev];
+    return MICA_OK;
+}
+
+int mica_w8a8_gemm_swiglu_quant_noalloc(const int8_t* A, long lda, const int8_t* Bgu, long ldb, const float* sa,
+                                        const float* sgu, const float* bias_gu, void* h_out, long ldh,
+                                        int8_t* q_out, long ldq, float* s_out, int M, int I, int K,
+                                        int round_mode, void* stream) {
+    if (M > MICA_NOALLOC_MAX_ROWS) return MICA_ERR_WORKSPACE;   // beyond the fixed scratch: refuse up front
+    int rc = check_device(nullptr);
+    if (rc) return rc;
+    void* scratch = nullptr;
+    if ((rc = noalloc_scratch(&scratch))) return rc;
+    // The shared entry point clears the rows it uses (cudaMemsetAsync, no allocation)
+    // before launching, so stale contents from the previous call do not leak in.
+    return mica_w8a8_gemm_swiglu_quant(A, lda, Bgu, ldb, sa, sgu, bias_gu, h_out, ldh, q_out, ldq, s_out, M, I, K,
+                                       round_mode, scratch, MICA_NOALLOC_SCRATCH_BYTES, stream);
+}
+
+// ---------------------------------------------------------------------------------------
 int mica_option_logits(const void* h, int h_dtype, long ldh, const void* gamma, int norm_style, float eps,
                        const float* rows, int n_rows, int D, const int* lo, const int* hi, float* logits, float* probs,
                        int B, void* stream) {
