@@ -362,16 +362,16 @@ def run_shape(args):
     sw = torch.rand(n, generator=g, device=dev) * 9e-3 + 1e-3
     q, s = torch.ops.mica.act_quant(x, None, 0)
     for _ in range(args.warmup):
-        torch.ops.mica.w8a8_gemm(q, s, w, sw, None, 0, args.block_n)
+        torch.ops.mica.w8a8_gemm(q, s, w, sw, None, 0, args.tile)
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
     for _ in range(args.steps):
         q, s = torch.ops.mica.act_quant(x, None, 0)
-        torch.ops.mica.w8a8_gemm(q, s, w, sw, None, 0, args.block_n)
+        torch.ops.mica.w8a8_gemm(q, s, w, sw, None, 0, args.tile)
     b.record()
     torch.cuda.synchronize()
     ms = a.elapsed_time(b) / args.steps
-    print(json.dumps({'shape': [m, n, k], 'block_n': args.block_n, 'ms_per_linear': round(ms, 4),
+    print(json.dumps({'shape': [m, n, k], 'tile': args.tile, 'ms_per_linear': round(ms, 4),
                       'tops_incl_quant': round(2 * m * n * k / ms / 1e9, 1)}), flush=True)
 
 
@@ -383,7 +383,7 @@ def main():
     ap.add_argument('--impl', choices=('mica', 'reference'), default='mica')
     ap.add_argument('--cpu-seconds', type=float, default=10.0)
     ap.add_argument('--shape', default=None, help='M,N,K: time one linear shape only (profiling)')
-    ap.add_argument('--block-n', type=int, default=0)
+    ap.add_argument('--tile', type=int, default=0, help='block_m*1000+block_n, 0 = library choice')
     args = ap.parse_args()
     if args.shape:
         run_shape(args)

@@ -82,6 +82,7 @@ typedef struct mica_caps {
     int supported;          /* 1 when this library's kernels run on the device          */
     int max_smem_optin;     /* bytes of opt-in shared memory per block                  */
     int abi_version;        /* MICA_ABI_VERSION                                         */
+    int pair_clusters;      /* co-resident CTA pairs for the 256-row GEMM tiles         */
 } mica_caps;
 
 #define MICA_ABI_VERSION 1
@@ -143,12 +144,15 @@ int mica_w8a8_gemm(const int8_t* A, long lda, const int8_t* B, long ldb,
                    void* C, int c_dtype, long ldc,
                    int M, int N, int K, void* stream);
 
-/* As mica_w8a8_gemm with an explicit tile: block_n in {64, 128, 256} (0 = table choice)
- * and max_ctas (0 = one persistent CTA per SM). Used by the tile tuner.                */
+/* As mica_w8a8_gemm with an explicit output tile, used by the tile tuner:
+ *   block_m 128 = one CTA per tile; 256 = a pair of CTAs on two SMs sharing each MMA
+ *           (tcgen05 cta_group::2), 0 = library choice;
+ *   block_n 64 / 128 / 256 (pairs: 128 / 256), 0 = library choice;
+ *   max_ctas caps the persistent grid (0 = all SMs / all co-resident pairs).             */
 int mica_w8a8_gemm_cfg(const int8_t* A, long lda, const int8_t* B, long ldb,
                        const float* sa, const float* sb, const float* bias,
                        void* C, int c_dtype, long ldc,
-                       int M, int N, int K, int block_n, int max_ctas, void* stream);
+                       int M, int N, int K, int block_m, int block_n, int max_ctas, void* stream);
 
 /* Fused MLP front half: gate_up W8A8 GEMM + SwiGLU + next-layer per-token quantisation.
  *   Bgu [2*I, K]: gate and up weight rows interleaved in groups of 16
@@ -209,6 +213,16 @@ int mica_option_logits(const void* h, int h_dtype, long ldh,
                        const float* rows, int n_rows, int D,
                        const int* lo, const int* hi,
                        float* logits, float* probs, int B, void* stream);
+
+/* Per-head RMSNorm of q and k followed by the rotary embedding, in place on the QKV GEMM
+ * output (bf16 rows [q: H*D | k: KV*D | v], row stride ld elements). Reproduces HF Qwen3's
+ * bf16 sequence: y = w * bf16(x * rsqrt(mean(x^2) + eps)), then
+ * bf16(bf16(y * cos) + bf16(rotate_half(y) * sin)). cos/sin: bf16 [positions, D];
+ * pos: int64 [S] token positions on the device, or NULL for pos0 + row index.
+ * D in {64, 128}. Replaces the q_norm / k_norm / apply_rotary_pos_emb torch ops around the
+ * QKV projection (the reference runs them in torch, v0.5/serving/lib/prefill_engine.py:308-324). */
+int mica_qk_norm_rope(void* qkv, long ld, const void* q_w, const void* k_w, const void* cos, const void* sin,
+                      const int64_t* pos, long pos0, int S, int H, int KV, int D, float eps, void* stream);
 
 /* Failure-detection self-test: launches one block that waits on a barrier nothing
  * ever arrives on, with a wait limit of limit_us microseconds. The kernel gives up,

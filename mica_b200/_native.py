@@ -54,6 +54,7 @@ class Caps(ctypes.Structure):
         ('supported', _I),
         ('max_smem_optin', _I),
         ('abi_version', _I),
+        ('pair_clusters', _I),
     ]
 
 
@@ -68,7 +69,7 @@ SIGNATURES = {
         [_P, _I, _L, _P, _L, _P, _I, _F, _P, _P, _L, _P, _L, _P, _L, _P, _I, _I, _I, _P],
     ),
     'mica_w8a8_gemm': (_I, [_P, _L, _P, _L, _P, _P, _P, _P, _I, _L, _I, _I, _I, _P]),
-    'mica_w8a8_gemm_cfg': (_I, [_P, _L, _P, _L, _P, _P, _P, _P, _I, _L, _I, _I, _I, _I, _I, _P]),
+    'mica_w8a8_gemm_cfg': (_I, [_P, _L, _P, _L, _P, _P, _P, _P, _I, _L, _I, _I, _I, _I, _I, _I, _P]),
     'mica_swiglu_workspace_bytes': (_Z, [_I]),
     'mica_w8a8_gemm_swiglu_quant': (
         _I,
@@ -79,6 +80,7 @@ SIGNATURES = {
         [_P, _L, _P, _L, _P, _P, _P, _P, _L, _P, _L, _P, _I, _I, _I, _I, _P],
     ),
     'mica_option_logits': (_I, [_P, _I, _L, _P, _I, _F, _P, _I, _I, _P, _P, _P, _P, _I, _P]),
+    'mica_qk_norm_rope': (_I, [_P, _L, _P, _P, _P, _P, _P, _L, _I, _I, _I, _I, _F, _P]),
     'mica_selftest_wait_timeout': (_I, [_P, _I, _P]),
 }
 

@@ -22,18 +22,20 @@ namespace mica {
 
 enum EpiKind { EPI_DEQUANT = 0, EPI_SWIGLU = 1 };
 
-template <int BN_>
+template <int BN_, int EW_ = 4>
 struct GemmShape {
     static constexpr int BM = 128;
     static constexpr int BN = BN_;
+    static constexpr int EW = EW_;                      // epilogue warps: 4, or 8 (two per TMEM lane quarter)
     static constexpr int BK = 128;                      // bytes (= int8 elements) of K per stage
     static constexpr int UMMA_K = 32;                   // K of one kind::i8 MMA
     static constexpr int A_BYTES = BM * BK;             // 16 KB
     static constexpr int B_BYTES = BN * BK;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr int EPI_WARPS = 4;
+    static constexpr int EPI_WARPS = EW;
     static constexpr int BOX_BYTES = 32 * 128;          // one 32-row x 128-byte store box
-    static constexpr int EPI_BYTES = EPI_WARPS * 2 * BOX_BYTES;
+    static constexpr int BOX_BUFS = EW == 4 ? 2 : 1;    // store boxes per epilogue warp
+    static constexpr int EPI_BYTES = EPI_WARPS * BOX_BUFS * BOX_BYTES;
     static constexpr int AUX_BYTES = 256;               // mbarriers, TMEM address, abort flag
     static constexpr int SMEM_OPTIN = 232448;           // sm_100 opt-in shared memory per block
     static constexpr int STAGES_RAW = (SMEM_OPTIN - 1024 - EPI_BYTES - AUX_BYTES) / STAGE_BYTES;
@@ -41,7 +43,8 @@ struct GemmShape {
     static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + AUX_BYTES;
     static constexpr int ACC_COLS = BN;                 // int32 accumulator columns per buffer
     static constexpr int TMEM_COLS = (2 * BN < 32) ? 32 : 2 * BN;
-    static constexpr int THREADS = 192;
+    static constexpr int THREADS = 64 + 32 * EW;
+    static_assert(EW == 4 || EW == 8, "epilogue warps");
     static_assert(STAGES >= 2, "not enough shared memory for a pipeline");
     static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256, "BN");
     static_assert(SMEM_BYTES <= SMEM_OPTIN, "smem");
@@ -78,11 +81,11 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t
                  : "memory");
 }
 
-template <int BN, int EPI, typename OutT>
-__global__ void __launch_bounds__(192, 1)
+template <int BN, int EPI, typename OutT, int EW = 4>
+__global__ void __launch_bounds__(64 + 32 * EW, 1)
 gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                const __grid_constant__ CUtensorMap tmap_c, const GemmArgs args) {
-    using S = GemmShape<BN>;
+    using S = GemmShape<BN, EW>;
     constexpr int STAGES = S::STAGES;
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -205,8 +208,10 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
         // ------------------------------- epilogue -----------------------------------
         const int q4 = warp & 3;                  // TMEM lane quarter this warp may access
         const int row_local = q4 * 32 + lane;
-        const int ew = warp - 2;                  // epilogue warp 0..3
-        uint8_t* my_boxes = smem_epi + ew * 2 * S::BOX_BYTES;
+        const int ew = warp - 2;                  // epilogue warp 0..EW-1
+        const int part = ew >> 2;                 // with 8 warps, two share a lane quarter
+        constexpr int PARTS = EW / 4;
+        uint8_t* my_boxes = smem_epi + ew * S::BOX_BUFS * S::BOX_BYTES;
         int box_count = 0;
         int local = 0;
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
@@ -228,9 +233,13 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
                 constexpr int CHUNKS_PER_BOX = COLS_PER_BOX / 32;
                 constexpr int BOXES = BN / COLS_PER_BOX;
 #pragma unroll 1
-                for (int bx = 0; bx < BOXES; ++bx, ++box_count) {
-                    uint8_t* box = my_boxes + (box_count & 1) * S::BOX_BYTES;
-                    if (lane == 0) tma_store_wait_read<1>();   // the store that used this box is done reading
+                for (int bx = part; bx < BOXES; bx += PARTS, ++box_count) {
+                    uint8_t* box = my_boxes + (box_count % S::BOX_BUFS) * S::BOX_BYTES;
+                    // the store that last used this box must have finished reading it
+                    if (lane == 0) {
+                        if constexpr (S::BOX_BUFS == 2) tma_store_wait_read<1>();
+                        else tma_store_wait_read<0>();
+                    }
                     __syncwarp();
                     const uint32_t box_row = smem_u32(box) + lane * 128;
 #pragma unroll
@@ -274,15 +283,16 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
                             }
                         }
                     }
-                    if (bx == BOXES - 1) {
-                        // accumulator fully read: hand the buffer back to the MMA warp
+                    if (bx + PARTS >= BOXES) {
+                        // this warp's last read of the accumulator: hand it back to the MMA warp
                         tc_fence_before();
                         mbar_arrive(&tempty_bar[acc]);
                     }
                     fence_proxy_async_smem();
                     __syncwarp();
                     if (lane == 0) {
-                        tma_store_2d(&tmap_c, box, n0 + bx * COLS_PER_BOX, m0 + q4 * 32);
+                        const int x = n0 + bx * COLS_PER_BOX, y = m0 + q4 * 32;
+                        if (x < N && y < M) tma_store_2d(&tmap_c, box, x, y);   // boxes past the edge hold nothing
                         tma_store_commit();
                     }
                 }
@@ -294,9 +304,12 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
                 constexpr int BOXES = BN / 128;
                 float amax = 0.f;
 #pragma unroll 1
-                for (int bx = 0; bx < BOXES; ++bx, ++box_count) {
-                    uint8_t* box = my_boxes + (box_count & 1) * S::BOX_BYTES;
-                    if (lane == 0) tma_store_wait_read<1>();
+                for (int bx = part; bx < BOXES; bx += PARTS, ++box_count) {
+                    uint8_t* box = my_boxes + (box_count % S::BOX_BUFS) * S::BOX_BYTES;
+                    if (lane == 0) {
+                        if constexpr (S::BOX_BUFS == 2) tma_store_wait_read<1>();
+                        else tma_store_wait_read<0>();
+                    }
                     __syncwarp();
                     const uint32_t box_row = smem_u32(box) + lane * 128;
 #pragma unroll
@@ -325,7 +338,10 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
                                 }
                                 g = bf16_round(g);
                                 u = bf16_round(u);
-                                const float act = bf16_round(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))));
+                                // silu in fp32 with branch-free intrinsics (few-ulp fp32 error,
+                                // below the bf16 rounding that follows), so the 16 independent
+                                // chains of a chunk interleave instead of serialising on slow paths
+                                const float act = bf16_round(__fdividef(g, 1.0f + __expf(-g)));
                                 const float h = bf16_round(__fmul_rn(act, u));
                                 amax = fmaxf(amax, fabsf(h));
                                 hv[e] = h;
@@ -339,14 +355,15 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
                                          p[4 * c + 3]);
                         }
                     }
-                    if (bx == BOXES - 1) {
+                    if (bx + PARTS >= BOXES) {
                         tc_fence_before();
                         mbar_arrive(&tempty_bar[acc]);
                     }
                     fence_proxy_async_smem();
                     __syncwarp();
                     if (lane == 0) {
-                        tma_store_2d(&tmap_c, box, n0 / 2 + bx * H_PER_BOX, m0 + q4 * 32);
+                        const int x = n0 / 2 + bx * H_PER_BOX, y = m0 + q4 * 32;
+                        if (x < N / 2 && y < M) tma_store_2d(&tmap_c, box, x, y);
                         tma_store_commit();
                     }
                 }
@@ -396,18 +413,23 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
             const float scale = __fdiv_rn(fmaxf(__uint_as_float(bits), 1e-8f), 127.0f);
             const __nv_bfloat16* hrow = args.h + static_cast<long>(row) * args.ldh;
             int8_t* qrow = args.q_out + static_cast<long>(row) * args.ldq;
-            for (int c = lane * 8; c < I; c += 32 * 8) {
-                const uint4 v = __ldcg(reinterpret_cast<const uint4*>(hrow + c));
-                const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
-                uint32_t out[2] = {0u, 0u};
+            // two 8-element vectors per lane per step: 16 independent divisions in flight
+            for (int c = lane * 8; c < I; c += 32 * 8 * 2) {
+                const int c2 = c + 32 * 8;
+                const bool has2 = c2 < I;
+                const uint4 v0 = __ldcg(reinterpret_cast<const uint4*>(hrow + c));
+                const uint4 v1 = has2 ? __ldcg(reinterpret_cast<const uint4*>(hrow + c2)) : make_uint4(0, 0, 0, 0);
+                const uint32_t w8[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+                uint32_t out[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    const uint32_t half = (w4[e >> 1] >> ((e & 1) * 16)) & 0xFFFFu;
+                for (int e = 0; e < 16; ++e) {
+                    const uint32_t half = (w8[e >> 1] >> ((e & 1) * 16)) & 0xFFFFu;
                     const float x = __uint_as_float(half << 16);
                     const int qv = quant_round(__fdiv_rn(x, scale), args.round_mode);
                     out[e >> 2] |= (static_cast<uint32_t>(qv) & 0xFFu) << ((e & 3) * 8);
                 }
                 *reinterpret_cast<uint2*>(qrow + c) = make_uint2(out[0], out[1]);
+                if (has2) *reinterpret_cast<uint2*>(qrow + c2) = make_uint2(out[2], out[3]);
             }
             if (lane == 0) args.s_out[row] = scale;
         }

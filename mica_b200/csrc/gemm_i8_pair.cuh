@@ -1,0 +1,285 @@
+// gemm_i8_pair.cuh -- W8A8 GEMM on CTA pairs (tcgen05 cta_group::2), 256 x BN output tiles.
+//
+// A cluster of two CTAs on two SMs computes one 256 x BN tile with a single stream of
+// tcgen05.mma.cta_group::2.kind::i8 instructions (256 x BN x 32 each) issued by the even
+// CTA. Each CTA loads 128 rows of A and BN/2 rows of B per stage into its own shared memory
+// (at identical offsets), so per SM the MMA reads 16 KB of A and 16 KB of B per 128-byte K
+// step instead of 16 + 32 KB in the single-CTA kernel: a third less shared-memory and L2
+// traffic for the same work, and room for six stages instead of four.
+//
+// Synchronisation (all waits bounded, as in gemm_i8.cuh):
+//   full[s]    even CTA only: both CTAs' TMA loads complete their bytes on it;
+//   empty[s]   per CTA: the even CTA's MMA commit arrives on both CTAs' copies;
+//   tfull[a]   per CTA: the even CTA's last commit of a tile arrives on both copies;
+//   tempty[a]  even CTA only: all 256 epilogue threads of the pair arrive on it.
+// Epilogue and semantics are those of gemm_i8_kernel (dequant, no FMA, TMA store).
+#pragma once
+
+#include "gemm_i8.cuh"
+
+namespace mica {
+
+template <int BN_>
+struct PairShape {
+    static constexpr int BN = BN_;
+    static constexpr int BM = 256;                      // rows per pair tile (128 per CTA)
+    static constexpr int BK = 128;
+    static constexpr int UMMA_K = 32;
+    static constexpr int A_BYTES = 128 * BK;            // this CTA's 128 rows
+    static constexpr int B_BYTES = (BN / 2) * BK;       // this CTA's half of B's rows
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int EPI_WARPS = 4;
+    static constexpr int BOX_BYTES = 32 * 128;
+    static constexpr int EPI_BYTES = EPI_WARPS * 2 * BOX_BYTES;
+    static constexpr int AUX_BYTES = 256;
+    static constexpr int SMEM_OPTIN = 232448;
+    static constexpr int STAGES_RAW = (SMEM_OPTIN - 1024 - EPI_BYTES - AUX_BYTES) / STAGE_BYTES;
+    static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
+    static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + AUX_BYTES;
+    static constexpr int ACC_COLS = BN;
+    static constexpr int TMEM_COLS = 2 * BN;
+    static constexpr int THREADS = 192;
+    static_assert(BN == 128 || BN == 256, "pair tile width");
+    static_assert(SMEM_BYTES <= SMEM_OPTIN, "smem");
+};
+
+template <int BN, typename OutT>
+__global__ void __launch_bounds__(192, 1)
+gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                    const __grid_constant__ CUtensorMap tmap_c, const GemmArgs args) {
+    using S = PairShape<BN>;
+    constexpr int STAGES = S::STAGES;
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();      // 0 = the CTA that issues the MMAs
+    const bool leader = rank == 0;
+
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw_addr = smem_u32(smem_raw);
+    uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+    uint8_t* smem_a = smem;
+    uint8_t* smem_b = smem + STAGES * S::A_BYTES;
+    uint8_t* smem_epi = smem_b + STAGES * S::B_BYTES;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem_epi + S::EPI_BYTES);
+    uint64_t* full_bar = bars;
+    uint64_t* empty_bar = bars + STAGES;
+    uint64_t* tfull_bar = bars + 2 * STAGES;
+    uint64_t* tempty_bar = bars + 2 * STAGES + 2;
+    uint64_t* drain_bar = bars + 2 * STAGES + 4;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
+    volatile uint32_t* abort_flag = tmem_slot + 1;
+
+    const int M = args.M, N = args.N, K = args.K;
+    const int num_m = (M + S::BM - 1) / S::BM;
+    const int num_n = (N + BN - 1) / BN;
+    const int num_tiles = num_m * num_n;
+    const int num_kb = (K + S::BK - 1) / S::BK;
+    const int cluster_id = blockIdx.x >> 1;
+    const int num_clusters = gridDim.x >> 1;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < STAGES; ++i) {
+            mbar_init(&full_bar[i], 1);
+            mbar_init(&empty_bar[i], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&tfull_bar[i], 1);
+            mbar_init(&tempty_bar[i], 2 * S::EPI_WARPS * 32);
+        }
+        mbar_init(drain_bar, 1);
+        *abort_flag = 0u;
+        fence_mbar_init();
+        tma_prefetch_desc(&tmap_a);
+        tma_prefetch_desc(&tmap_b);
+        tma_prefetch_desc(&tmap_c);
+    }
+    if (warp == 1) tmem_alloc_pair(tmem_slot, S::TMEM_COLS);
+    tc_fence_before();
+    cluster_sync();            // barriers of both CTAs initialised before any remote arrive
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ------------------------------- TMA producer (both CTAs) --------------------
+        if (lane == 0) {
+            uint32_t it = 0;
+            bool ok = true;
+            const uint64_t pol_b = policy_evict_last();
+            const uint64_t pol_a = policy_evict_normal();  // activations: re-read by every N tile
+            for (int tile = cluster_id; tile < num_tiles && ok; tile += num_clusters) {
+                const int m0 = (tile / num_n) * S::BM;
+                const int n0 = (tile % num_n) * BN;
+                for (int kb = 0; kb < num_kb; ++kb, ++it) {
+                    const int st = it % STAGES;
+                    const uint32_t ph = (it / STAGES) & 1u;
+                    if (!mbar_wait(&empty_bar[st], ph ^ 1u, abort_flag, MICA_DEV_TIMEOUT_PRODUCER)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t full0 = map_to_rank(smem_u32(&full_bar[st]), 0);
+                    if (leader) mbar_arrive_expect_tx(&full_bar[st], 2 * S::STAGE_BYTES);
+                    tma_load_2d_pair(smem_a + st * S::A_BYTES, &tmap_a, full0, kb * S::BK,
+                                     m0 + static_cast<int>(rank) * 128, pol_a);
+                    tma_load_2d_pair(smem_b + st * S::B_BYTES, &tmap_b, full0, kb * S::BK,
+                                     n0 + static_cast<int>(rank) * (BN / 2), pol_b);
+                }
+            }
+            if (leader) {
+                // Drain: the pair's last loads of each stage land before shared memory goes away.
+                const uint32_t first = it > static_cast<uint32_t>(STAGES) ? it - STAGES : 0u;
+                for (uint32_t j = first; j < it; ++j)
+                    mbar_wait(&full_bar[j % STAGES], (j / STAGES) & 1u, abort_flag, MICA_DEV_TIMEOUT_DRAIN);
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        // ------------------------------- MMA issuer (even CTA) -----------------------
+        if (leader) {
+            constexpr uint32_t idesc = idesc_i8(S::BM, BN);
+            const uint32_t a_base = smem_u32(smem_a);
+            const uint32_t b_base = smem_u32(smem_b);
+            uint32_t it = 0;
+            int local = 0;
+            bool ok = true;
+            for (int tile = cluster_id; tile < num_tiles && ok; tile += num_clusters, ++local) {
+                const int acc = local & 1;
+                const uint32_t acc_ph = (local >> 1) & 1;
+                bool w = true;
+                if (lane == 0) w = mbar_wait(&tempty_bar[acc], acc_ph ^ 1u, abort_flag, MICA_DEV_TIMEOUT_MMA);
+                if (!__shfl_sync(0xffffffffu, w, 0)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + acc * S::ACC_COLS;
+                for (int kb = 0; kb < num_kb; ++kb, ++it) {
+                    const int st = it % STAGES;
+                    const uint32_t ph = (it / STAGES) & 1u;
+                    if (lane == 0) w = mbar_wait(&full_bar[st], ph, abort_flag, MICA_DEV_TIMEOUT_MMA);
+                    if (!__shfl_sync(0xffffffffu, w, 0)) { ok = false; break; }
+                    tc_fence_after();
+                    if (lane == 0) {
+                        const uint32_t a_addr = a_base + st * S::A_BYTES;
+                        const uint32_t b_addr = b_base + st * S::B_BYTES;
+#pragma unroll
+                        for (int k = 0; k < S::BK / S::UMMA_K; ++k) {
+                            mma_i8_pair(d_tmem, smem_desc_k128(a_addr + k * S::UMMA_K),
+                                        smem_desc_k128(b_addr + k * S::UMMA_K), idesc, (kb | k) != 0 ? 1u : 0u);
+                        }
+                        const uint32_t e = smem_u32(&empty_bar[st]);
+                        mma_commit_pair(map_to_rank(e, 0));
+                        mma_commit_pair(map_to_rank(e, 1));
+                        if (kb == num_kb - 1) {
+                            const uint32_t f = smem_u32(&tfull_bar[acc]);
+                            mma_commit_pair(map_to_rank(f, 0));
+                            mma_commit_pair(map_to_rank(f, 1));
+                        }
+                    }
+                    __syncwarp();
+                }
+            }
+            if (lane == 0) {
+                mma_commit_pair(map_to_rank(smem_u32(drain_bar), 0));
+                mbar_wait(drain_bar, 0, abort_flag, MICA_DEV_TIMEOUT_DRAIN);
+            }
+            __syncwarp();
+        }
+    } else {
+        // ------------------------------- epilogue (both CTAs) ------------------------
+        const int q4 = warp & 3;
+        const int row_local = static_cast<int>(rank) * 128 + q4 * 32 + lane;
+        const int ew = warp - 2;
+        uint8_t* my_boxes = smem_epi + ew * 2 * S::BOX_BYTES;
+        int box_count = 0;
+        int local = 0;
+        constexpr int COLS_PER_BOX = 128 / static_cast<int>(sizeof(OutT));
+        constexpr int CHUNKS_PER_BOX = COLS_PER_BOX / 32;
+        constexpr int BOXES = BN / COLS_PER_BOX;
+        for (int tile = cluster_id; tile < num_tiles; tile += num_clusters, ++local) {
+            const int m0 = (tile / num_n) * S::BM;
+            const int n0 = (tile % num_n) * BN;
+            const int acc = local & 1;
+            const uint32_t acc_ph = (local >> 1) & 1;
+            bool w = true;
+            if (lane == 0) w = mbar_wait(&tfull_bar[acc], acc_ph, abort_flag, MICA_DEV_TIMEOUT_EPILOGUE);
+            if (!__shfl_sync(0xffffffffu, w, 0)) break;
+            tc_fence_after();
+            const int grow = m0 + row_local;
+            const float sa_v = grow < M ? args.sa[grow] : 0.f;
+            const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q4 * 32) << 16) + acc * S::ACC_COLS;
+#pragma unroll 1
+            for (int bx = 0; bx < BOXES; ++bx, ++box_count) {
+                uint8_t* box = my_boxes + (box_count & 1) * S::BOX_BYTES;
+                if (lane == 0) tma_store_wait_read<1>();
+                __syncwarp();
+                const uint32_t box_row = smem_u32(box) + lane * 128;
+#pragma unroll
+                for (int cc = 0; cc < CHUNKS_PER_BOX; ++cc) {
+                    const int col0 = bx * COLS_PER_BOX + cc * 32;
+                    const int gcol = n0 + col0 + lane;
+                    const float sb_l = gcol < N ? args.sb[gcol] : 0.f;
+                    const float bias_l = (args.bias != nullptr && gcol < N) ? args.bias[gcol] : 0.f;
+                    uint32_t r[32];
+                    tmem_ld_32x32b_x32(t_row + col0, r);
+                    tmem_ld_wait();
+                    float y[32];
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const float sbj = __shfl_sync(0xffffffffu, sb_l, j);
+                        y[j] = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[j])), sa_v), sbj);
+                    }
+                    if (args.bias != nullptr) {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) y[j] = __fadd_rn(y[j], __shfl_sync(0xffffffffu, bias_l, j));
+                    }
+                    if constexpr (sizeof(OutT) == 2) {
+                        uint32_t p[16];
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) {
+                            if constexpr (std::is_same<OutT, __half>::value) p[j] = pack_f16(y[2 * j], y[2 * j + 1]);
+                            else p[j] = pack_bf16(y[2 * j], y[2 * j + 1]);
+                        }
+#pragma unroll
+                        for (int c = 0; c < 4; ++c) {
+                            const int chunk = cc * 4 + c;
+                            st_shared_v4(box_row + ((chunk ^ (lane & 7)) << 4), p[4 * c], p[4 * c + 1], p[4 * c + 2],
+                                         p[4 * c + 3]);
+                        }
+                    } else {
+#pragma unroll
+                        for (int c = 0; c < 8; ++c) {
+                            st_shared_v4(box_row + ((c ^ (lane & 7)) << 4), __float_as_uint(y[4 * c]),
+                                         __float_as_uint(y[4 * c + 1]), __float_as_uint(y[4 * c + 2]),
+                                         __float_as_uint(y[4 * c + 3]));
+                        }
+                    }
+                }
+                if (bx == BOXES - 1) {
+                    tc_fence_before();
+                    mbar_arrive_cluster(map_to_rank(smem_u32(&tempty_bar[acc]), 0));
+                }
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    const int x = n0 + bx * COLS_PER_BOX, y = m0 + static_cast<int>(rank) * 128 + q4 * 32;
+                    if (x < N && y < M) tma_store_2d(&tmap_c, box, x, y);   // boxes past the edge hold nothing
+                    tma_store_commit();
+                }
+            }
+        }
+        if (lane == 0) tma_store_wait_all<0>();
+        __syncwarp();
+    }
+
+    // A CTA that gave up may still have TMA loads in flight that count on the other CTA's
+    // barrier; give them time to land before the pair's shared memory is released.
+    if (*abort_flag) {
+        const unsigned long long t0 = global_ns();
+        while (global_ns() - t0 < 200000ull) __nanosleep(1000);
+    }
+    tc_fence_before();
+    cluster_sync();            // the even CTA's MMAs read this CTA's smem: leave together
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_free_pair(tmem_base, S::TMEM_COLS);
+    }
+}
+
+}  // namespace mica

@@ -15,8 +15,10 @@
 
 #include "common.cuh"
 #include "gemm_i8.cuh"
+#include "gemm_i8_pair.cuh"
 #include "quant.cuh"
 #include "readout.cuh"
+#include "qk_rope.cuh"
 
 using namespace mica;
 
@@ -112,29 +114,29 @@ static int launch_status() {
 static size_t dt_size(int dt) { return dt == MICA_DT_FP32 ? 4 : 2; }
 
 // ---- GEMM kernel registry ------------------------------------------------------------
-template <int BN, int EPI, typename OutT>
+template <int BN, int EPI, typename OutT, int EW = 4>
 static int gemm_prepare() {
     int dev = 0;
     cudaGetDevice(&dev);
     static std::atomic<uint64_t> done{0};  // one bit per device
     const uint64_t bit = 1ull << (dev & 63);
     if (done.load(std::memory_order_acquire) & bit) return MICA_OK;
-    cudaError_t e = cudaFuncSetAttribute(gemm_i8_kernel<BN, EPI, OutT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         GemmShape<BN>::SMEM_BYTES);
+    cudaError_t e = cudaFuncSetAttribute(gemm_i8_kernel<BN, EPI, OutT, EW>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, GemmShape<BN, EW>::SMEM_BYTES);
     if (e != cudaSuccess) { set_cuda_error(e); return MICA_ERR_CUDA; }
     done.fetch_or(bit, std::memory_order_release);
     return MICA_OK;
 }
 
-template <int BN, int EPI, typename OutT>
+template <int BN, int EPI, typename OutT, int EW = 4>
 static int gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const GemmArgs& args,
                        int grid, bool cooperative, cudaStream_t stream) {
-    int rc = gemm_prepare<BN, EPI, OutT>();
+    int rc = gemm_prepare<BN, EPI, OutT, EW>();
     if (rc) return rc;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(GemmShape<BN>::THREADS);
-    cfg.dynamicSmemBytes = GemmShape<BN>::SMEM_BYTES;
+    cfg.blockDim = dim3(GemmShape<BN, EW>::THREADS);
+    cfg.dynamicSmemBytes = GemmShape<BN, EW>::SMEM_BYTES;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     if (cooperative) {
@@ -143,20 +145,85 @@ static int gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUten
         cfg.attrs = attr;
         cfg.numAttrs = 1;
     }
-    cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_i8_kernel<BN, EPI, OutT>, ta, tb, tc, args);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_i8_kernel<BN, EPI, OutT, EW>, ta, tb, tc, args);
     if (e != cudaSuccess) { set_cuda_error(e); return MICA_ERR_CUDA; }
     return launch_status();
 }
 
-// Tile choice: the widest tile that still gives every SM work; a pinned table in the
-// Python layer may override it (mica_w8a8_gemm_cfg).
-static int pick_bn(int M, int N, int sms) {
+// ---- CTA-pair kernels ---------------------------------------------------------------------
+// Co-resident clusters of two per device (pairs of SMs the scheduler can place together).
+static std::atomic<int> g_pair_clusters[kMaxDev];
+
+template <int BN, typename OutT>
+static int pair_prepare(int* max_clusters) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    static std::atomic<uint64_t> done{0};
+    const uint64_t bit = 1ull << (dev & 63);
+    if (!(done.load(std::memory_order_acquire) & bit)) {
+        cudaError_t e = cudaFuncSetAttribute(gemm_i8_pair_kernel<BN, OutT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             PairShape<BN>::SMEM_BYTES);
+        if (e != cudaSuccess) { set_cuda_error(e); return MICA_ERR_CUDA; }
+        if (g_pair_clusters[dev].load() == 0) {
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3(2 * 512);
+            cfg.blockDim = dim3(PairShape<BN>::THREADS);
+            cfg.dynamicSmemBytes = PairShape<BN>::SMEM_BYTES;
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeClusterDimension;
+            attr[0].val.clusterDim.x = 2;
+            attr[0].val.clusterDim.y = 1;
+            attr[0].val.clusterDim.z = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            int n = 0;
+            e = cudaOccupancyMaxActiveClusters(&n, gemm_i8_pair_kernel<BN, OutT>, &cfg);
+            if (e != cudaSuccess || n < 1) {
+                set_cuda_error(e != cudaSuccess ? e : cudaErrorInvalidConfiguration);
+                return MICA_ERR_CUDA;
+            }
+            g_pair_clusters[dev].store(n);
+        }
+        done.fetch_or(bit, std::memory_order_release);
+    }
+    *max_clusters = g_pair_clusters[dev].load();
+    return MICA_OK;
+}
+
+template <int BN, typename OutT>
+static int pair_launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const GemmArgs& args,
+                       long tiles, int max_ctas, cudaStream_t stream) {
+    int clusters = 0;
+    int rc = pair_prepare<BN, OutT>(&clusters);
+    if (rc) return rc;
+    if (max_ctas > 0 && clusters > max_ctas / 2) clusters = max_ctas / 2 > 0 ? max_ctas / 2 : 1;
+    if (tiles < clusters) clusters = static_cast<int>(tiles);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * clusters);
+    cfg.blockDim = dim3(PairShape<BN>::THREADS);
+    cfg.dynamicSmemBytes = PairShape<BN>::SMEM_BYTES;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_i8_pair_kernel<BN, OutT>, ta, tb, tc, args);
+    if (e != cudaSuccess) { set_cuda_error(e); return MICA_ERR_CUDA; }
+    return launch_status();
+}
+
+// Tile choice when the caller (or the pinned table in the Python layer) gives none,
+// from the measured sweep over the 4B model's projection shapes: the single-CTA 128 x 256
+// tile wins whenever it fills a wave of SMs; below that 128 x 128, then 128 x 64.
+static void pick_tile(int M, int N, int sms, int* bm, int* bn) {
     const long m_blocks = (M + 127) / 128;
     const long t256 = m_blocks * ((N + 255) / 256);
     const long t128 = m_blocks * ((N + 127) / 128);
-    if (t256 >= 2L * sms) return 256;
-    if (t128 >= sms) return 128;
-    return 64;
+    *bm = 128;
+    *bn = t256 >= sms ? 256 : (2 * t128 >= sms ? 128 : 64);
 }
 
 }  // namespace mica_host
@@ -187,6 +254,16 @@ int mica_query(int device, mica_caps* caps) {
         return MICA_ERR_CUDA;
     }
     caps->supported = (caps->cc_major == 10 && caps->cc_minor == 0 && caps->max_smem_optin >= 232448) ? 1 : 0;
+    if (caps->supported) {
+        int prev = 0;
+        if ((e = cudaGetDevice(&prev)) != cudaSuccess || (e = cudaSetDevice(device)) != cudaSuccess) {
+            set_cuda_error(e);
+            return MICA_ERR_CUDA;
+        }
+        int rc = pair_prepare<256, __nv_bfloat16>(&caps->pair_clusters);
+        cudaSetDevice(prev);
+        if (rc) return rc;
+    }
     return MICA_OK;
 }
 
@@ -206,9 +283,21 @@ int mica_preload(int* n_kernels) {
     PREP(64, EPI_DEQUANT, float)
     PREP(128, EPI_DEQUANT, float)
     PREP(256, EPI_DEQUANT, float)
-    PREP(128, EPI_SWIGLU, __nv_bfloat16)
-    PREP(256, EPI_SWIGLU, __nv_bfloat16)
 #undef PREP
+    if ((rc = gemm_prepare<128, EPI_SWIGLU, __nv_bfloat16, 8>()) != MICA_OK) return rc;
+    if ((rc = gemm_prepare<256, EPI_SWIGLU, __nv_bfloat16, 8>()) != MICA_OK) return rc;
+    n += 2;
+    int clusters = 0;
+#define PREP_PAIR(BN, T)                                               \
+    if ((rc = pair_prepare<BN, T>(&clusters)) != MICA_OK) return rc; \
+    ++n;
+    PREP_PAIR(128, __nv_bfloat16)
+    PREP_PAIR(256, __nv_bfloat16)
+    PREP_PAIR(128, __half)
+    PREP_PAIR(256, __half)
+    PREP_PAIR(128, float)
+    PREP_PAIR(256, float)
+#undef PREP_PAIR
     if (n_kernels) *n_kernels = n;
     return MICA_OK;
 }
@@ -309,31 +398,55 @@ static int gemm_dispatch_out(const CUtensorMap& ta, const CUtensorMap& tb, const
 }
 
 int mica_w8a8_gemm_cfg(const int8_t* A, long lda, const int8_t* B, long ldb, const float* sa, const float* sb,
-                       const float* bias, void* C, int c_dtype, long ldc, int M, int N, int K, int block_n,
-                       int max_ctas, void* stream) {
+                       const float* bias, void* C, int c_dtype, long ldc, int M, int N, int K, int block_m,
+                       int block_n, int max_ctas, void* stream) {
     int rc = gemm_checks(A, lda, B, ldb, sa, sb, bias, C, c_dtype, ldc, M, N, K);
     if (rc) return rc;
+    if (block_m != 0 && block_m != 128 && block_m != 256) return MICA_ERR_ARG;
     if (block_n != 0 && block_n != 64 && block_n != 128 && block_n != 256) return MICA_ERR_ARG;
+    if (block_m == 256 && block_n == 64) return MICA_ERR_ARG;
     if (max_ctas < 0) return MICA_ERR_ARG;
     int sms = 0;
     if ((rc = check_device(&sms))) return rc;
     if (M == 0) return MICA_OK;
-    const int bn = block_n ? block_n : pick_bn(M, N, sms);
+    int bm = block_m, bn = block_n;
+    if (bm == 0 && bn == 0) {
+        pick_tile(M, N, sms, &bm, &bn);
+    } else if (bm == 0) {
+        bm = 128;
+    } else if (bn == 0) {
+        int pm = 0;
+        pick_tile(M, N, sms, &pm, &bn);
+        if (bm == 256 && bn == 64) bn = 128;
+    }
     CUtensorMap ta, tb, tc;
     const CUtensorMapDataType cdt = c_dtype == MICA_DT_BF16   ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                     : c_dtype == MICA_DT_FP16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
                                                               : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
     const uint32_t es = static_cast<uint32_t>(dt_size(c_dtype));
+    // A CTA of a pair loads 128 rows of A and bn/2 rows of B.
+    const uint32_t b_box = bm == 256 ? static_cast<uint32_t>(bn / 2) : static_cast<uint32_t>(bn);
     if ((rc = make_tmap_2d(&ta, A, CU_TENSOR_MAP_DATA_TYPE_UINT8, K, M, lda, 128, 128)) ||
-        (rc = make_tmap_2d(&tb, B, CU_TENSOR_MAP_DATA_TYPE_UINT8, K, N, ldb, 128, bn)) ||
+        (rc = make_tmap_2d(&tb, B, CU_TENSOR_MAP_DATA_TYPE_UINT8, K, N, ldb, 128, b_box)) ||
         (rc = make_tmap_2d(&tc, C, cdt, N, M, ldc * es, 128 / es, 32)))
         return rc;
     GemmArgs g = {};
     g.sa = sa; g.sb = sb; g.bias = bias; g.M = M; g.N = N; g.K = K;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (bm == 256) {
+        const long tiles = static_cast<long>((M + 255) / 256) * ((N + bn - 1) / bn);
+        if (bn == 256) {
+            if (c_dtype == MICA_DT_BF16) return pair_launch<256, __nv_bfloat16>(ta, tb, tc, g, tiles, max_ctas, st);
+            if (c_dtype == MICA_DT_FP16) return pair_launch<256, __half>(ta, tb, tc, g, tiles, max_ctas, st);
+            return pair_launch<256, float>(ta, tb, tc, g, tiles, max_ctas, st);
+        }
+        if (c_dtype == MICA_DT_BF16) return pair_launch<128, __nv_bfloat16>(ta, tb, tc, g, tiles, max_ctas, st);
+        if (c_dtype == MICA_DT_FP16) return pair_launch<128, __half>(ta, tb, tc, g, tiles, max_ctas, st);
+        return pair_launch<128, float>(ta, tb, tc, g, tiles, max_ctas, st);
+    }
     const long tiles = static_cast<long>((M + 127) / 128) * ((N + bn - 1) / bn);
     int grid = static_cast<int>(tiles < sms ? tiles : sms);
     if (max_ctas > 0 && grid > max_ctas) grid = max_ctas;
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (bn == 256) return gemm_dispatch_out<256>(ta, tb, tc, g, c_dtype, grid, st);
     if (bn == 128) return gemm_dispatch_out<128>(ta, tb, tc, g, c_dtype, grid, st);
     return gemm_dispatch_out<64>(ta, tb, tc, g, c_dtype, grid, st);
@@ -341,7 +454,7 @@ int mica_w8a8_gemm_cfg(const int8_t* A, long lda, const int8_t* B, long ldb, con
 
 int mica_w8a8_gemm(const int8_t* A, long lda, const int8_t* B, long ldb, const float* sa, const float* sb,
                    const float* bias, void* C, int c_dtype, long ldc, int M, int N, int K, void* stream) {
-    return mica_w8a8_gemm_cfg(A, lda, B, ldb, sa, sb, bias, C, c_dtype, ldc, M, N, K, 0, 0, stream);
+    return mica_w8a8_gemm_cfg(A, lda, B, ldb, sa, sb, bias, C, c_dtype, ldc, M, N, K, 0, 0, 0, stream);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -388,8 +501,8 @@ int mica_w8a8_gemm_swiglu_quant(const int8_t* A, long lda, const int8_t* Bgu, lo
     g.h = static_cast<const __nv_bfloat16*>(h_out); g.ldh = ldh; g.q_out = q_out; g.ldq = ldq; g.s_out = s_out;
     const long tiles = static_cast<long>((M + 127) / 128) * ((N + bn - 1) / bn);
     const int grid = static_cast<int>(tiles < sms ? tiles : sms);
-    if (bn == 256) return gemm_launch<256, EPI_SWIGLU, __nv_bfloat16>(ta, tb, th, g, grid, true, st);
-    return gemm_launch<128, EPI_SWIGLU, __nv_bfloat16>(ta, tb, th, g, grid, true, st);
+    if (bn == 256) return gemm_launch<256, EPI_SWIGLU, __nv_bfloat16, 8>(ta, tb, th, g, grid, true, st);
+    return gemm_launch<128, EPI_SWIGLU, __nv_bfloat16, 8>(ta, tb, th, g, grid, true, st);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -479,6 +592,30 @@ int mica_option_logits(const void* h, int h_dtype, long ldh, const void* gamma, 
         return launch_status();
     }
     return MICA_OK;
+}
+
+// ---------------------------------------------------------------------------------------
+int mica_qk_norm_rope(void* qkv, long ld, const void* q_w, const void* k_w, const void* cos, const void* sin,
+                      const int64_t* pos, long pos0, int S, int H, int KV, int D, float eps, void* stream) {
+    if (!qkv || !cos || !sin || (H > 0 && !q_w) || (KV > 0 && !k_w)) return MICA_ERR_ARG;
+    if (S < 0 || H < 0 || KV < 0 || (D != 64 && D != 128) || ld < static_cast<long>(H + KV) * D || pos0 < 0)
+        return MICA_ERR_SHAPE;
+    if (!aligned16(qkv) || (ld * 2) % 16) return MICA_ERR_ALIGN;
+    int rc = check_device(nullptr);
+    if (rc) return rc;
+    const long warps = static_cast<long>(S) * (H + KV);
+    if (warps == 0) return MICA_OK;
+    if (warps > (1L << 31) * 8 / 256 * 32) return MICA_ERR_RANGE;
+    QkRopeArgs a = {};
+    a.qkv = static_cast<__nv_bfloat16*>(qkv); a.ld = ld;
+    a.q_w = static_cast<const __nv_bfloat16*>(q_w); a.k_w = static_cast<const __nv_bfloat16*>(k_w);
+    a.cos = static_cast<const __nv_bfloat16*>(cos); a.sin = static_cast<const __nv_bfloat16*>(sin);
+    a.pos = reinterpret_cast<const long*>(pos); a.pos0 = pos0; a.S = S; a.H = H; a.KV = KV; a.eps = eps;
+    const unsigned blocks = static_cast<unsigned>((warps * 32 + 255) / 256);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (D == 128) qk_norm_rope_kernel<128><<<blocks, 256, 0, st>>>(a);
+    else qk_norm_rope_kernel<64><<<blocks, 256, 0, st>>>(a);
+    return launch_status();
 }
 
 // ---------------------------------------------------------------------------------------

@@ -157,8 +157,7 @@ def mm_i8(qx, sx, qw, sw, bias=None, out_dtype=torch.bfloat16):
         return _miss('align')
     if m == 0:
         return qx.new_empty((0, n), dtype=out_dtype)
-    bn = tiles.block_n(n, k, m)
-    y = torch.ops.mica.w8a8_gemm(qx, sx, qw, sw, bias, ops.DTYPE_CODE[out_dtype], bn)
+    y = torch.ops.mica.w8a8_gemm(qx, sx, qw, sw, bias, ops.DTYPE_CODE[out_dtype], tiles.tile(n, k, m))
     _launched()
     return y
 

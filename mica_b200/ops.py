@@ -9,9 +9,10 @@ shapes without running anything.
     torch.ops.mica.act_quant(x, inv, round_mode)                       -> (q, s)
     torch.ops.mica.rmsnorm_quant(x, residual, gamma, inv, eps, style, round_mode, want_y)
                                                                         -> (q, s, y, sum)
-    torch.ops.mica.w8a8_gemm(qx, sx, qw, sw, bias, out_dtype, block_n)  -> y
+    torch.ops.mica.w8a8_gemm(qx, sx, qw, sw, bias, out_dtype, tile)     -> y
     torch.ops.mica.gemm_swiglu_quant(qx, sx, qw_gu, sw_gu, bias, round_mode) -> (h, q, s)
     torch.ops.mica.option_logits(h, rows, gamma, lo, hi, eps, style)    -> (logits, probs)
+    torch.ops.mica.qk_norm_rope(qkv, q_w, k_w, cos, sin, pos, pos0, heads, kv_heads, eps)  (in place)
 """
 from __future__ import annotations
 
@@ -101,18 +102,20 @@ def _(x, residual, gamma, inv, eps, style, round_mode, want_y, want_q):
 # ---------------------------------------------------------------------------------------
 @torch.library.custom_op('mica::w8a8_gemm', mutates_args=())
 def w8a8_gemm(qx: torch.Tensor, sx: torch.Tensor, qw: torch.Tensor, sw: torch.Tensor, bias: Optional[torch.Tensor],
-              out_dtype: int, block_n: int) -> torch.Tensor:
+              out_dtype: int, tile: int) -> torch.Tensor:
+    """tile = block_m * 1000 + block_n (e.g. 256256 = CTA pair, 256 x 256), 0 = library choice."""
     m, k = qx.shape
     n = qw.shape[0]
     out = torch.empty((m, n), dtype=OUT_DTYPES[out_dtype], device=qx.device)
     with _on(qx):
         N.call('mica_w8a8_gemm_cfg', qx.data_ptr(), qx.stride(0), qw.data_ptr(), qw.stride(0), sx.data_ptr(),
-               sw.data_ptr(), _ptr(bias), out.data_ptr(), out_dtype, out.stride(0), m, n, k, block_n, 0, _stream(qx))
+               sw.data_ptr(), _ptr(bias), out.data_ptr(), out_dtype, out.stride(0), m, n, k, tile // 1000, tile % 1000,
+               0, _stream(qx))
     return out
 
 
 @w8a8_gemm.register_fake
-def _(qx, sx, qw, sw, bias, out_dtype, block_n):
+def _(qx, sx, qw, sw, bias, out_dtype, tile):
     return qx.new_empty((qx.shape[0], qw.shape[0]), dtype=OUT_DTYPES[out_dtype])
 
 
@@ -161,3 +164,19 @@ def option_logits(h: torch.Tensor, rows: torch.Tensor, gamma: Optional[torch.Ten
 def _(h, rows, gamma, lo, hi, eps, style):
     b, r = h.shape[0], rows.shape[0]
     return h.new_empty((b, r), dtype=torch.float32), h.new_empty((b, r), dtype=torch.float32)
+
+
+# ---------------------------------------------------------------------------------------
+@torch.library.custom_op('mica::qk_norm_rope', mutates_args=('qkv',))
+def qk_norm_rope(qkv: torch.Tensor, q_w: Optional[torch.Tensor], k_w: Optional[torch.Tensor], cos: torch.Tensor,
+                 sin: torch.Tensor, pos: Optional[torch.Tensor], pos0: int, heads: int, kv_heads: int,
+                 eps: float) -> None:
+    d = cos.shape[1]
+    with _on(qkv):
+        N.call('mica_qk_norm_rope', qkv.data_ptr(), qkv.stride(0), _ptr(q_w), _ptr(k_w), cos.data_ptr(),
+               sin.data_ptr(), _ptr(pos), pos0, qkv.shape[0], heads, kv_heads, d, eps, _stream(qkv))
+
+
+@qk_norm_rope.register_fake
+def _(qkv, q_w, k_w, cos, sin, pos, pos0, heads, kv_heads, eps):
+    return None

@@ -1,0 +1,342 @@
+"""Prefill scorer for a dense Qwen3-style decoder on the W8A8 kernels.
+
+This is the model-level caller of the hot path: it restates what the reference's
+PrefillEngine does for one request (v0.5/serving/lib/prefill_engine.py:274-339 run /
+final_hidden, :385-418 capture / replay) on the dense decoder of BASELINE configs 3-4
+(Qwen3-4B dims: hidden 2560, 32 q / 8 kv heads x 128, FFN 9728, 36 layers).
+
+Per layer, five launches of this library plus attention:
+  rmsnorm_quant(prev_out, residual)  -> new residual stream + int8 codes (fused prologue)
+  w8a8 GEMM QKV (tcgen05)            -> q, k, v  (q/k RMSNorm + RoPE in torch, bf16, as HF)
+  attention: torch SDPA (cuDNN/flash), causal, GQA
+  act_quant(attn) + w8a8 GEMM O
+  rmsnorm_quant(o, residual)         -> codes for the MLP
+  gate_up GEMM + SwiGLU + requant    -> codes for down (one cooperative launch)
+  w8a8 GEMM down
+The last layer computes K/V for every row but Q, attention, O and the MLP only for the
+scored row (prefill_engine.py:306-339), then the fused final norm + gathered lm_head GEMV
++ option softmax (release_runtime.py:302-306, :509-522).
+
+Graphs: capture() records the whole prefill for a 64-token bucket with a static id
+buffer and a `limit` row (the real length), like the reference's per-bucket graphs; rows
+past `limit` are padding that no real row attends to.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import torch
+import torch.nn.functional as F
+
+from . import _native as N
+from . import int8_kernels as K
+from . import ops  # noqa: F401
+from .int8_runtime import interleave_gate_up, quant_weight
+
+BUCKET = 64
+
+
+@dataclass
+class DecoderConfig:
+    hidden: int = 2560
+    inter: int = 9728
+    layers: int = 36
+    heads: int = 32
+    kv_heads: int = 8
+    head_dim: int = 128
+    vocab: int = 151936
+    eps: float = 1e-6
+    rope_theta: float = 1e6
+    tie_embeddings: bool = True
+
+    @property
+    def q_dim(self):
+        return self.heads * self.head_dim
+
+    @property
+    def kv_dim(self):
+        return self.kv_heads * self.head_dim
+
+
+@dataclass
+class Layer:
+    in_norm: torch.Tensor
+    qkv_w: torch.Tensor
+    qkv_s: torch.Tensor
+    q_norm: torch.Tensor
+    k_norm: torch.Tensor
+    o_w: torch.Tensor
+    o_s: torch.Tensor
+    post_norm: torch.Tensor
+    gu_w: torch.Tensor
+    gu_s: torch.Tensor
+    down_w: torch.Tensor
+    down_s: torch.Tensor
+
+
+@dataclass
+class Decoder:
+    cfg: DecoderConfig
+    embed: torch.Tensor                      # bf16 [vocab, hidden]
+    layers: list = field(default_factory=list)
+    final_norm: torch.Tensor = None          # bf16 [hidden]
+    lm_head: torch.Tensor = None             # bf16 [vocab, hidden] (None = tied to embed)
+
+    @property
+    def device(self):
+        return self.embed.device
+
+
+# ---------------------------------------------------------------------------------------
+def _q(w):
+    q, s = quant_weight(w)
+    return q.contiguous(), s.contiguous()
+
+
+def from_hf_state(state: dict, cfg: DecoderConfig, device) -> Decoder:
+    """Builds the decoder from a HF Qwen3ForCausalLM state dict (bf16), quantising every
+    projection per output row exactly as the reference's QLinear does (no smoothing)."""
+    def t(name):
+        return state[name].to(device)
+
+    layers = []
+    for i in range(cfg.layers):
+        p = f'model.layers.{i}.'
+        qkv = torch.cat([t(p + 'self_attn.q_proj.weight'), t(p + 'self_attn.k_proj.weight'),
+                         t(p + 'self_attn.v_proj.weight')]).float()
+        qkv_w, qkv_s = _q(qkv)
+        o_w, o_s = _q(t(p + 'self_attn.o_proj.weight').float())
+        g_w, g_s = _q(t(p + 'mlp.gate_proj.weight').float())
+        u_w, u_s = _q(t(p + 'mlp.up_proj.weight').float())
+        d_w, d_s = _q(t(p + 'mlp.down_proj.weight').float())
+        layers.append(Layer(
+            in_norm=t(p + 'input_layernorm.weight').to(torch.bfloat16).contiguous(),
+            qkv_w=qkv_w, qkv_s=qkv_s,
+            q_norm=t(p + 'self_attn.q_norm.weight').to(torch.bfloat16).contiguous(),
+            k_norm=t(p + 'self_attn.k_norm.weight').to(torch.bfloat16).contiguous(),
+            o_w=o_w, o_s=o_s,
+            post_norm=t(p + 'post_attention_layernorm.weight').to(torch.bfloat16).contiguous(),
+            gu_w=interleave_gate_up(g_w, u_w), gu_s=interleave_gate_up(g_s, u_s),
+            down_w=d_w, down_s=d_s))
+    lm = state.get('lm_head.weight')
+    return Decoder(cfg=cfg, embed=t('model.embed_tokens.weight').to(torch.bfloat16).contiguous(), layers=layers,
+                   final_norm=t('model.norm.weight').to(torch.bfloat16).contiguous(),
+                   lm_head=None if (lm is None or cfg.tie_embeddings) else lm.to(device).to(torch.bfloat16))
+
+
+def random_decoder(cfg: DecoderConfig, device, seed: int = 0, std: float = 0.02) -> Decoder:
+    """Random-init decoder of the given dims, generated on the device: bf16 weights N(0, std)
+    quantised per output row (as converting a random-init HF model would), norm weights
+    N(1, 0.1)."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    H, I = cfg.hidden, cfg.inter
+
+    def w(n, k):
+        return _q(torch.randn(n, k, generator=g, device=device) * std)
+
+    def gamma(n):
+        return (1 + 0.1 * torch.randn(n, generator=g, device=device)).to(torch.bfloat16)
+
+    layers = []
+    for _ in range(cfg.layers):
+        qkv_w, qkv_s = w(cfg.q_dim + 2 * cfg.kv_dim, H)
+        o_w, o_s = w(H, cfg.q_dim)
+        g_w, g_s = w(I, H)
+        u_w, u_s = w(I, H)
+        d_w, d_s = w(H, I)
+        layers.append(Layer(in_norm=gamma(H), qkv_w=qkv_w, qkv_s=qkv_s, q_norm=gamma(cfg.head_dim),
+                            k_norm=gamma(cfg.head_dim), o_w=o_w, o_s=o_s, post_norm=gamma(H),
+                            gu_w=interleave_gate_up(g_w, u_w), gu_s=interleave_gate_up(g_s, u_s), down_w=d_w,
+                            down_s=d_s))
+        del g_w, u_w
+    embed = (torch.randn(cfg.vocab, H, generator=g, device=device) * std).to(torch.bfloat16)
+    return Decoder(cfg=cfg, embed=embed, layers=layers, final_norm=gamma(H))
+
+
+# ---------------------------------------------------------------------------------------
+def rope_tables(cfg: DecoderConfig, n: int, device):
+    """cos/sin [n, head_dim] in bf16, computed in fp32 as HF Qwen3RotaryEmbedding does."""
+    d = cfg.head_dim
+    inv = 1.0 / (cfg.rope_theta ** (torch.arange(0, d, 2, dtype=torch.int64, device=device).float() / d))
+    pos = torch.arange(n, device=device).float()
+    freqs = (inv[:, None] @ pos[None, :]).t()
+    emb = torch.cat((freqs, freqs), dim=-1)
+    return emb.cos().to(torch.bfloat16), emb.sin().to(torch.bfloat16)
+
+
+class Prefill:
+    """Scores requests on a Decoder: ids -> option probabilities of the last position."""
+
+    def __init__(self, model: Decoder, option_ids, max_len: int = 32768, attn_backends=None):
+        self.m = model
+        cfg = model.cfg
+        dev = model.device
+        self.cfg = cfg
+        head = model.lm_head if model.lm_head is not None else model.embed
+        ids = torch.as_tensor(option_ids, device=dev, dtype=torch.long)
+        self.rows = head.index_select(0, ids).float().contiguous()      # release_runtime.py:302
+        self.cos, self.sin = rope_tables(cfg, max_len, dev)
+        self.max_len = max_len
+        self.scale = cfg.head_dim ** -0.5
+        self.graphs = {}
+        self.pool = None
+        if attn_backends is None:
+            from torch.nn.attention import SDPBackend
+            attn_backends = [SDPBackend.CUDNN_ATTENTION, SDPBackend.FLASH_ATTENTION, SDPBackend.EFFICIENT_ATTENTION]
+        self.backends = attn_backends
+
+    # ---- pieces ------------------------------------------------------------------------
+    def _norm_quant(self, x, w, residual=None):
+        q, s, _, summed = torch.ops.mica.rmsnorm_quant(x, residual, w, None, self.cfg.eps, N.NORM_WEIGHT,
+                                                        K._round_code(), False, True)
+        return q, s, (summed if residual is not None else x)
+
+    def _gemm(self, q, s, w, sw):
+        return torch.ops.mica.w8a8_gemm(q, s, w, sw, None, 0, K.tiles.tile(w.shape[0], w.shape[1], q.shape[0]))
+
+    def _attention(self, q, k, v, causal, mask=None):
+        from torch.nn.attention import sdpa_kernel
+        qh, kh, vh = q.transpose(0, 1)[None], k.transpose(0, 1)[None], v.transpose(0, 1)[None]
+        with sdpa_kernel(self.backends):
+            o = F.scaled_dot_product_attention(qh, kh, vh, attn_mask=mask, is_causal=causal and mask is None,
+                                               scale=self.scale, enable_gqa=True)
+        return o[0].transpose(0, 1).reshape(q.shape[0], -1).contiguous()
+
+    def _mlp(self, q, s, lay):
+        _, qh, sh = torch.ops.mica.gemm_swiglu_quant(q, s, lay.gu_w, lay.gu_s, None, K._round_code())
+        return self._gemm(qh, sh, lay.down_w, lay.down_s)
+
+    # ---- forward -------------------------------------------------------------------------
+    def hidden_last(self, ids: torch.Tensor, limit: torch.Tensor = None, last_only: bool = True):
+        """Runs the decoder over ids [S] and returns the last real row's hidden state
+        (before the final norm) as bf16 [1, hidden]. `limit` (int tensor [1]) marks the real
+        length when ids are padded to a bucket; keys at or past it are masked."""
+        cfg, m = self.cfg, self.m
+        S = ids.shape[0]
+        cos, sin = self.cos[:S], self.sin[:S]
+        h = F.embedding(ids, m.embed)
+        prev = None
+        nl = len(m.layers)
+        for li, lay in enumerate(m.layers):
+            q8, s8, h = self._norm_quant(prev if prev is not None else h, lay.in_norm,
+                                         h if prev is not None else None)
+            if li == nl - 1 and last_only:
+                return self._last_layer(q8, s8, h, lay, cos, sin, limit)
+            qkv = self._gemm(q8, s8, lay.qkv_w, lay.qkv_s)
+            torch.ops.mica.qk_norm_rope(qkv, lay.q_norm, lay.k_norm, self.cos, self.sin, None, 0, cfg.heads,
+                                        cfg.kv_heads, cfg.eps)
+            q, k, v = qkv.split([cfg.q_dim, cfg.kv_dim, cfg.kv_dim], dim=1)
+            attn = self._attention(q.view(S, cfg.heads, cfg.head_dim), k.view(S, cfg.kv_heads, cfg.head_dim),
+                                   v.view(S, cfg.kv_heads, cfg.head_dim), causal=True)
+            qa, sa = torch.ops.mica.act_quant(attn, None, K._round_code())
+            o = self._gemm(qa, sa, lay.o_w, lay.o_s)
+            q8, s8, h = self._norm_quant(o, lay.post_norm, h)
+            prev = self._mlp(q8, s8, lay)
+        # full path: pick the last real row after the final residual add
+        out = (h + prev)
+        return self._pick(out, limit)
+
+    def _pick(self, t, limit):
+        if limit is None:
+            return t[-1:]
+        idx = (limit - 1).view(1, 1).expand(1, t.shape[1])
+        return t.gather(0, idx)
+
+    def _last_layer(self, q8, s8, h, lay, cos, sin, limit):
+        """K/V for every row, Q / attention / O / MLP for the scored row only."""
+        cfg = self.cfg
+        S = q8.shape[0]
+        qd, kd = cfg.q_dim, cfg.kv_dim
+        kv = self._gemm(q8, s8, lay.qkv_w[qd:], lay.qkv_s[qd:])
+        torch.ops.mica.qk_norm_rope(kv, None, lay.k_norm, self.cos, self.sin, None, 0, 0, cfg.kv_heads, cfg.eps)
+        k, v = kv.split([kd, kd], dim=1)
+        if limit is None:
+            row_q8, row_s8, res = q8[-1:], s8[-1:], h[-1:]
+            pos = torch.full((1,), S - 1, dtype=torch.long, device=q8.device)
+            mask = None
+        else:
+            li = (limit - 1).view(1)
+            row_q8 = q8.index_select(0, li)
+            row_s8 = s8.index_select(0, li)
+            res = h.index_select(0, li)
+            pos = li.to(torch.long)
+            keys = torch.arange(S, device=q8.device)
+            mask = torch.where(keys[None, :] < limit.view(1, 1), 0.0, float('-inf')).to(torch.bfloat16)
+            mask = mask.view(1, 1, 1, S)
+        q = self._gemm(row_q8, row_s8, lay.qkv_w[:qd], lay.qkv_s[:qd])
+        torch.ops.mica.qk_norm_rope(q, lay.q_norm, None, self.cos, self.sin, pos, 0, cfg.heads, 0, cfg.eps)
+        attn = self._attention(q.view(1, cfg.heads, cfg.head_dim), k.view(S, cfg.kv_heads, cfg.head_dim),
+                               v.view(S, cfg.kv_heads, cfg.head_dim), causal=False, mask=mask)
+        qa, sa = torch.ops.mica.act_quant(attn, None, K._round_code())
+        o = self._gemm(qa, sa, lay.o_w, lay.o_s)
+        q8r, s8r, res = self._norm_quant(o, lay.post_norm, res)
+        d = self._mlp(q8r, s8r, lay)
+        return res + d
+
+    def probs(self, h_last: torch.Tensor, lo=None, hi=None):
+        """Final norm + gathered lm_head GEMV + option softmax (one library call)."""
+        return torch.ops.mica.option_logits(h_last.contiguous(), self.rows, self.m.final_norm, lo, hi, self.cfg.eps,
+                                            N.NORM_WEIGHT)
+
+    @torch.no_grad()
+    def score(self, ids, lo=None, hi=None, graphs: bool = True):
+        """ids: 1-D int64 tensor on the device; lo/hi: the option slice (ints, default all
+        rows). Uses a captured graph when the request's bucket has one, else runs eagerly.
+        Returns (logits, probs) fp32 [1, n_rows]."""
+        n = int(ids.shape[0])
+        if graphs and self.bucket(n) in self.graphs:
+            return self.replay(ids, lo, hi)
+        dev = ids.device
+        lo_t = None if lo is None else torch.tensor([int(lo)], dtype=torch.int32, device=dev)
+        hi_t = None if hi is None else torch.tensor([int(hi)], dtype=torch.int32, device=dev)
+        if lo_t is not None and hi_t is None:
+            hi_t = torch.tensor([self.rows.shape[0]], dtype=torch.int32, device=dev)
+        if hi_t is not None and lo_t is None:
+            lo_t = torch.zeros(1, dtype=torch.int32, device=dev)
+        return self.probs(self.hidden_last(ids), lo_t, hi_t)
+
+    # ---- CUDA graphs ------------------------------------------------------------------------
+    def bucket(self, n: int) -> int:
+        return -(-n // BUCKET) * BUCKET
+
+    @torch.no_grad()
+    def capture(self, length: int):
+        """Captures the prefill of a `length`-token bucket (a multiple of 64)."""
+        if length % BUCKET or length > self.max_len:
+            raise ValueError(f'bucket {length} is not a multiple of {BUCKET} within {self.max_len}')
+        dev = self.m.device
+        ids = torch.zeros(length, dtype=torch.long, device=dev)
+        limit = torch.full((1,), length, dtype=torch.long, device=dev)
+        lo = torch.zeros(1, dtype=torch.int32, device=dev)
+        hi = torch.full((1,), self.rows.shape[0], dtype=torch.int32, device=dev)
+        s = torch.cuda.Stream(device=dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                self.probs(self.hidden_last(ids, limit), lo, hi)
+        torch.cuda.current_stream(dev).wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        if self.pool is None:
+            self.pool = torch.cuda.graph_pool_handle()     # all buckets share one pool, as in the reference
+        with torch.cuda.graph(g, pool=self.pool):
+            out = self.probs(self.hidden_last(ids, limit), lo, hi)
+        self.graphs[length] = {'graph': g, 'ids': ids, 'limit': limit, 'lo': lo, 'hi': hi, 'out': out}
+        return g
+
+    @torch.no_grad()
+    def replay(self, ids, lo=None, hi=None):
+        n = int(ids.shape[0])
+        L = self.bucket(n)
+        e = self.graphs[L]
+        e['ids'][:n].copy_(ids)
+        if n < L:
+            e['ids'][n:].zero_()
+        e['limit'].fill_(n)
+        e['lo'].fill_(0 if lo is None else int(lo))
+        e['hi'].fill_(self.rows.shape[0] if hi is None else int(hi))
+        e['graph'].replay()
+        return e['out']
+
+    def release(self):
+        self.graphs.clear()
+        self.pool = None

@@ -6,8 +6,9 @@ GEMM_CLASSES (v0.5/serving/lib/int8_kernels.py:356, :381-385); its FLA autotune 
 pinned or re-tuned on the device and persisted in --state-dir (lib/kernel_state.py:111-256,
 lib/release_runtime.py:1260-1333).
 
-Here a key is (N, K, M-class) and the value the GEMM's output-tile width block_n
-(64 / 128 / 256; 0 = let the library choose). `pinned` ships with the package
+Here a key is (N, K, M-class) and the value the GEMM's output tile, coded
+block_m * 1000 + block_n: 128064 / 128128 / 128256 for one CTA per tile, 256128 / 256256
+for a CTA pair sharing each MMA (0 = let the library choose). `pinned` ships with the package
 (tiles_sm100a.json); `full` sweeps block_n on the device for the shapes in use and writes
 the winners to <state_dir>/tiles_sm100a.json, which later runs load first.
 """
@@ -22,7 +23,7 @@ HERE = Path(__file__).resolve().parent
 PINNED = HERE / 'tiles_sm100a.json'
 STATE_NAME = 'tiles_sm100a.json'
 CLASSES = ((128, 's'), (384, 'm'), (1024, 'n'))
-CHOICES = (64, 128, 256)
+CHOICES = (128064, 128128, 128256, 256128, 256256)
 
 _TABLE = None
 _LOCK = threading.Lock()
@@ -66,13 +67,13 @@ def set_state_dir(path) -> None:
         _TABLE = None
 
 
-def block_n(n: int, k: int, m: int) -> int:
+def tile(n: int, k: int, m: int) -> int:
     return table().get(key(n, k, m), 0)
 
 
 def tune(shapes, device='cuda', reps: int = 20, state_dir=None) -> dict:
-    """Sweeps block_n for each (N, K, M) on the device; returns {key: best} and, with a
-    state dir, persists it there. Times with CUDA events on the current stream."""
+    """Sweeps the tile choices for each (N, K, M) on the device; returns {key: best} and,
+    with a state dir, persists it there. Times with CUDA events on the current stream."""
     import torch
 
     from . import ops

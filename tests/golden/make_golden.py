@@ -194,6 +194,48 @@ def selftest_cases(g):
                       qw=q.qweight.numpy(), sw=q.wscale.numpy(), x=bits(x), y=bits(y))}
 
 
+MODEL_DIMS = dict(hidden_size=128, intermediate_size=256, num_hidden_layers=3, num_attention_heads=2,
+                  num_key_value_heads=1, head_dim=64, vocab_size=512, rms_norm_eps=1e-6, rope_theta=1e6,
+                  tie_word_embeddings=True)
+
+
+@torch.no_grad()
+def model_cases(g):
+    """A tiny dense Qwen3 decoder scored the reference way: every projection converted by
+    the reference's int8_runtime.convert (QLinear 'emulate': quant_act half-even + exact int
+    GEMM + dequant), last hidden state of the final norm, fp32 linear over gathered label
+    rows (release_runtime.py:302-306), softmax over the option slice (:509-522)."""
+    from transformers import Qwen3Config, Qwen3ForCausalLM
+    cfg = Qwen3Config(**MODEL_DIMS)
+    cfg._attn_implementation = 'eager'
+    torch.manual_seed(20261202)
+    model = Qwen3ForCausalLM(cfg).eval()
+    for name, prm in model.named_parameters():
+        if name.endswith('norm.weight'):
+            prm.data = 1 + 0.1 * torch.randn(prm.shape, generator=g)
+    model = model.to(torch.bfloat16)
+    state = {k: v.clone() for k, v in model.state_dict().items()}
+    replaced, _ = rt.convert(model.model, None, 'emulate')
+    assert replaced == 7 * cfg.num_hidden_layers
+    options = torch.randperm(cfg.vocab_size, generator=g)[:40]
+    weight = model.get_output_embeddings().weight.detach().index_select(0, options).float().clone()
+    out = {'state/' + k: bits(v) for k, v in state.items() if v.dtype == torch.bfloat16}
+    out['options'] = options.numpy().astype(np.int64)
+    for i, n in enumerate((37, 100)):
+        ids = torch.randint(0, cfg.vocab_size, (n,), generator=g)
+        hid = model.model(ids[None]).last_hidden_state[:, -1]
+        z = torch.nn.functional.linear(hid.float(), weight).float()
+        lo, hi = (2, 2 + 17) if i == 0 else (0, 40)
+        p = torch.zeros_like(z)
+        p[:, lo:hi] = z[:, lo:hi].softmax(-1)
+        out[f'ids{i}'] = ids.numpy().astype(np.int64)
+        out[f'hidden{i}'] = bits(hid)
+        out[f'logits{i}'] = z.numpy()
+        out[f'probs{i}'] = p.numpy()
+        out[f'slice{i}'] = np.array([lo, hi], np.int32)
+    return {'m': out}
+
+
 def save(name, cases):
     flat = {f'{c}/{k}': v for c, d in cases.items() for k, v in d.items()}
     np.savez_compressed(HERE / f'{name}.npz', **flat)
@@ -207,3 +249,4 @@ if __name__ == '__main__':
     save('norm', norm_cases(g))
     save('readout', readout_cases(g))
     save('selftest', selftest_cases(g))
+    save('model', model_cases(g))

@@ -91,16 +91,19 @@ def test_gemm_golden(K, case):
     assert np.array_equal(y.cpu().view(torch.int16).numpy().view(np.uint16), g[f'{case}/y_qlinear'])
 
 
-@pytest.mark.parametrize('bn', [64, 128, 256])
-@pytest.mark.parametrize('m,n', [(1, 64), (3, 256), (130, 192), (200, 512), (1500, 320)])
-def test_gemm_int32_accumulators_exact(K, m, n, bn):
+TILES = [128064, 128128, 128256, 256128, 256256]   # block_m * 1000 + block_n
+
+
+@pytest.mark.parametrize('tile', TILES)
+@pytest.mark.parametrize('m,n', [(1, 64), (3, 256), (130, 192), (200, 512), (1500, 320), (513, 1024)])
+def test_gemm_int32_accumulators_exact(K, m, n, tile):
     """K=1024 keeps |acc| < 2^24, so float(acc) in the fp32 output is the exact int32."""
     k = 1024
-    g = torch.Generator().manual_seed(m + n + bn)
+    g = torch.Generator().manual_seed(m + n + tile)
     qx = torch.randint(-127, 128, (m, k), generator=g, dtype=torch.int8)
     qw = torch.randint(-127, 128, (n, k), generator=g, dtype=torch.int8)
     one_m, one_n = torch.ones(m), torch.ones(n)
-    y = torch.ops.mica.w8a8_gemm(qx.cuda(), one_m.cuda(), qw.cuda(), one_n.cuda(), None, 2, bn)
+    y = torch.ops.mica.w8a8_gemm(qx.cuda(), one_m.cuda(), qw.cuda(), one_n.cuda(), None, 2, tile)
     acc = O.int_gemm_exact(qx.numpy(), qw.numpy())
     assert np.array_equal(y.cpu().numpy().astype(np.int64), acc.astype(np.int64))
 
@@ -121,6 +124,23 @@ def test_gemm_random_vs_oracle(K, m, n, k, out):
     ref = O.dequant_out(O.int_gemm_exact(qx.numpy(), qw.numpy()), sx.numpy(), sw.numpy(),
                         None if bias is None else bias.numpy(), out=out)
     assert np.array_equal(to_np(y.float()), ref)
+
+
+@pytest.mark.parametrize('tile', TILES)
+@pytest.mark.parametrize('out', [0, 1, 2])
+@pytest.mark.parametrize('m,n,k', [(4096, 6144, 2560), (777, 2560, 9728), (256, 19456, 2560)])
+def test_gemm_tiles_bit_exact_vs_oracle(K, m, n, k, tile, out):
+    g = torch.Generator().manual_seed(m + n + k + tile + out)
+    qx = torch.randint(-127, 128, (m, k), generator=g, dtype=torch.int8)
+    qw = torch.randint(-127, 128, (n, k), generator=g, dtype=torch.int8)
+    sx = torch.rand(m, generator=g) * 0.05 + 1e-3
+    sw = torch.rand(n, generator=g) * 9e-3 + 1e-3
+    bias = torch.randn(n, generator=g) * 0.1
+    y = torch.ops.mica.w8a8_gemm(qx.cuda(), sx.cuda(), qw.cuda(), sw.cuda(), bias.cuda(), out, tile)
+    ref = O.dequant_out(O.int_gemm_exact(qx.numpy(), qw.numpy()), sx.numpy(), sw.numpy(), bias.numpy(),
+                        out=('bf16', 'fp16', 'fp32')[out])
+    assert np.array_equal(to_np(y.float()), ref)
+    assert dev_error() == 0
 
 
 def test_gemm_misses_match_reference_contract(K):

@@ -1,0 +1,126 @@
+"""Prefill scoring on the W8A8 kernels: option probabilities against the reference's own
+scoring of the same tiny Qwen3 model (tests/golden/model.npz, made by running the
+reference's int8_runtime.convert + readout), plus size-independent checks at full dims."""
+import numpy as np
+import pytest
+import torch
+
+from conftest import golden
+
+pytestmark = pytest.mark.gpu
+
+TINY = dict(hidden=128, inter=256, layers=3, heads=2, kv_heads=1, head_dim=64, vocab=512, eps=1e-6,
+            rope_theta=1e6, tie_embeddings=True)
+
+
+def _bf16(a):
+    return torch.from_numpy(a.view(np.int16)).view(torch.bfloat16)
+
+
+@pytest.fixture(scope='module')
+def tiny():
+    from mica_b200 import prefill as P
+    g = golden('model')
+    state = {k[len('m/state/'):]: _bf16(g[k]) for k in g.files if k.startswith('m/state/')}
+    cfg = P.DecoderConfig(**TINY)
+    model = P.from_hf_state(state, cfg, torch.device('cuda'))
+    return P.Prefill(model, torch.from_numpy(g['m/options']), max_len=512), g
+
+
+@pytest.mark.parametrize('i', [0, 1])
+def test_tiny_model_probs_match_reference(tiny, i):
+    import mica_b200.int8_kernels as K
+    pf, g = tiny
+    ids = torch.from_numpy(g[f'm/ids{i}']).cuda()
+    lo, hi = (int(v) for v in g[f'm/slice{i}'])
+    K.ROUND['mode'] = 'half_even'      # the reference's QLinear 'emulate' path rounds half to even
+    try:
+        z, p = pf.score(ids, lo, hi, graphs=False)
+        z_full, p_full = pf.probs(pf.hidden_last(ids, last_only=False), torch.tensor([lo], dtype=torch.int32,
+                                  device='cuda'), torch.tensor([hi], dtype=torch.int32, device='cuda'))
+    finally:
+        K.ROUND['mode'] = 'half_away'
+    ref_p, ref_z = g[f'm/probs{i}'], g[f'm/logits{i}']
+    assert np.abs(p.cpu().numpy() - ref_p).max() < 1e-3
+    assert np.abs(z.cpu().numpy() - ref_z).max() < 2e-2 * max(1.0, float(np.abs(ref_z).max()))
+    assert np.abs(p_full.cpu().numpy() - ref_p).max() < 1e-3
+    assert abs(float(p.sum()) - 1.0) < 1e-5
+
+
+def test_tiny_graph_replay_matches_eager(tiny):
+    pf, g = tiny
+    ids = torch.from_numpy(g['m/ids1']).cuda()          # 100 tokens -> bucket 128
+    z_e, p_e = pf.score(ids, 0, 40, graphs=False)
+    pf.capture(128)
+    z_g, p_g = (t.clone() for t in pf.score(ids, 0, 40))
+    assert torch.allclose(p_g, p_e, atol=1e-3, rtol=0)
+    # a second request through the same graph (other length, other slice)
+    ids2 = torch.from_numpy(g['m/ids0']).cuda()
+    z2, p2 = (t.clone() for t in pf.score(ids2, 2, 19))
+    z2e, p2e = pf.score(ids2, 2, 19, graphs=False)
+    assert torch.allclose(p2, p2e, atol=1e-3, rtol=0)
+    assert float(p2[0, :2].abs().sum()) == 0.0 and float(p2[0, 19:].abs().sum()) == 0.0
+    pf.release()
+
+
+def test_full_dims_last_row_path_matches_full_path():
+    """4B dims (2 layers): the last-layer row restriction gives the full computation's row."""
+    from mica_b200 import prefill as P
+    cfg = P.DecoderConfig(layers=2, vocab=4096)
+    model = P.random_decoder(cfg, torch.device('cuda'), seed=3)
+    options = torch.arange(2, 259)
+    pf = P.Prefill(model, options, max_len=4096)
+    ids = torch.randint(0, cfg.vocab, (1500,), generator=torch.Generator().manual_seed(5)).cuda()
+    z1, p1 = pf.score(ids, graphs=False)
+    z2, p2 = pf.probs(pf.hidden_last(ids, last_only=False))
+    assert torch.isfinite(p1).all()
+    assert abs(float(p1.sum()) - 1.0) < 1e-4
+    assert torch.allclose(p1, p2, atol=1e-3, rtol=0)
+
+
+def test_full_dims_36_layers_scores_finite_and_deterministic():
+    from mica_b200 import prefill as P
+    cfg = P.DecoderConfig(vocab=8192)
+    model = P.random_decoder(cfg, torch.device('cuda'), seed=11)
+    pf = P.Prefill(model, torch.arange(0, 257), max_len=4096)
+    ids = torch.randint(0, cfg.vocab, (4000,), generator=torch.Generator().manual_seed(6)).cuda()
+    a = pf.score(ids, 2, 257, graphs=False)[1].clone()
+    b = pf.score(ids, 2, 257, graphs=False)[1].clone()
+    assert torch.isfinite(a).all() and abs(float(a.sum()) - 1.0) < 1e-4
+    assert torch.equal(a, b)
+
+
+def _hf_qk(x, w, cos, sin, eps):
+    """HF Qwen3 q_norm/k_norm + apply_rotary_pos_emb as torch bf16 ops (the reference)."""
+    xf = x.float()
+    n = (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)).to(x.dtype)
+    y = w * n
+    h = y.shape[-1] // 2
+    rot = torch.cat((-y[..., h:], y[..., :h]), dim=-1)
+    return (y * cos[:, None, :]) + (rot * sin[:, None, :])
+
+
+@pytest.mark.parametrize('S,H,KV', [(1, 32, 8), (333, 32, 8), (2048, 4, 2)])
+def test_qk_norm_rope_matches_hf_torch_ops(S, H, KV):
+    from mica_b200 import ops  # noqa: F401
+    from mica_b200 import prefill as P
+    D = 128
+    g = torch.Generator(device='cuda').manual_seed(S + H)
+    qkv = (torch.randn(S, (H + 2 * KV) * D, generator=g, device='cuda') * 3).to(torch.bfloat16)
+    qw = (1 + 0.1 * torch.randn(D, generator=g, device='cuda')).to(torch.bfloat16)
+    kw = (1 + 0.1 * torch.randn(D, generator=g, device='cuda')).to(torch.bfloat16)
+    cfg = P.DecoderConfig(head_dim=D)
+    cos, sin = P.rope_tables(cfg, 4096, torch.device('cuda'))
+    pos0 = 100
+    ref_q = _hf_qk(qkv[:, :H * D].view(S, H, D), qw, cos[pos0:pos0 + S], sin[pos0:pos0 + S], 1e-6)
+    ref_k = _hf_qk(qkv[:, H * D:(H + KV) * D].view(S, KV, D), kw, cos[pos0:pos0 + S], sin[pos0:pos0 + S], 1e-6)
+    v_before = qkv[:, (H + KV) * D:].clone()
+    torch.ops.mica.qk_norm_rope(qkv, qw, kw, cos, sin, None, pos0, H, KV, 1e-6)
+    got_q = qkv[:, :H * D].view(S, H, D)
+    got_k = qkv[:, H * D:(H + KV) * D].view(S, KV, D)
+    for got, ref in ((got_q, ref_q), (got_k, ref_k)):
+        # the rotation adds two rounded terms; near cancellation a 1-ulp difference in the
+        # normalised input is many ulps of the small sum, so compare values, not ulps
+        assert torch.allclose(got.float(), ref.float(), rtol=1e-2, atol=2e-2)
+        assert float((got != ref).float().mean()) < 0.01
+    assert torch.equal(qkv[:, (H + KV) * D:], v_before)

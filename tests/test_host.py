@@ -123,11 +123,11 @@ def test_tile_table_keys_use_reference_m_classes(tmp_path):
     from mica_b200 import tiles
     assert [tiles.m_class(m) for m in (1, 128, 129, 384, 385, 1024, 1025)] == ['s', 's', 'm', 'm', 'n', 'n', 'l']
     assert tiles.key(6144, 2560, 4096) == 'mm|N6144|K2560|cl'
-    (tmp_path / tiles.STATE_NAME).write_text('{"format": "mica-tiles/1", "entries": {"mm|N64|K64|cs": 128}}')
+    (tmp_path / tiles.STATE_NAME).write_text('{"format": "mica-tiles/1", "entries": {"mm|N64|K64|cs": 256128}}')
     tiles.set_state_dir(tmp_path)
     try:
-        assert tiles.block_n(64, 64, 7) == 128
-        assert tiles.block_n(64, 64, 700) == 0
+        assert tiles.tile(64, 64, 7) == 256128
+        assert tiles.tile(64, 64, 700) == 0
     finally:
         tiles.set_state_dir(None)
 
@@ -136,3 +136,23 @@ def test_native_errors_name_the_status():
     from mica_b200 import _native as N
     with pytest.raises(N.NativeError, match='ERR_SHAPE'):
         N.check('mica_x', 2)
+
+
+def test_decoder_from_hf_state_quantises_like_reference_qlinear():
+    """The golden tiny model's weights, converted on CPU, give the reference QLinear codes."""
+    from conftest import golden
+    from mica_b200 import prefill as P
+    g = golden('model')
+    bf = lambda a: torch.from_numpy(a.view(np.int16)).view(torch.bfloat16)  # noqa: E731
+    state = {k[len('m/state/'):]: bf(g[k]) for k in g.files if k.startswith('m/state/')}
+    cfg = P.DecoderConfig(hidden=128, inter=256, layers=3, heads=2, kv_heads=1, head_dim=64, vocab=512)
+    m = P.from_hf_state(state, cfg, torch.device('cpu'))
+    assert len(m.layers) == 3 and m.lm_head is None
+    lay = m.layers[1]
+    assert lay.qkv_w.shape == (256, 128) and lay.gu_w.shape == (512, 128) and lay.down_w.shape == (128, 256)
+    q_ref, s_ref = O.quant_weight(state['model.layers.1.self_attn.k_proj.weight'].float().numpy())
+    assert np.array_equal(lay.qkv_w[128:192].numpy(), q_ref) and np.array_equal(lay.qkv_s[128:192].numpy(), s_ref)
+    g_ref, _ = O.quant_weight(state['model.layers.1.mlp.gate_proj.weight'].float().numpy())
+    assert np.array_equal(lay.gu_w[:16].numpy(), g_ref[:16]) and np.array_equal(lay.gu_w[32:48].numpy(), g_ref[16:32])
+    cos, sin = P.rope_tables(cfg, 16, torch.device('cpu'))
+    assert cos.shape == (16, 64) and cos.dtype == torch.bfloat16 and float(cos[0, 0]) == 1.0
