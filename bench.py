@@ -7,7 +7,7 @@ M in {256, 2048, 8192, 32768} tokens. One step = the whole sweep (16 linears,
 43264 * 201.85 MOP = 8.733 TOP of GEMM work). Synthetic seeded data: activations bf16
 N(0,1), int8 weights uniform in [-127, 127], per-channel scales uniform in [1e-3, 1e-2].
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mica|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mica|reference] [--skip-model]
 
 value  : GEMM TOPS of the sweep, inputs resident in HBM, one CUDA-graph replay per step
          timed with CUDA events (L2 flushed between steps by a 256 MiB write outside
@@ -17,6 +17,9 @@ e2e    : the same sweep through the public API (QLinear-style calls) from pinned
          timed region.
 roofline: the GEMM kernel alone (per-launch CUDA events, averaged over the sweep's
          shapes) against 2 x the measured bf16 dense peak (B200 dense int8 = 2 x bf16).
+other_configs: BASELINE config 2 (fused MLP chain, us per chain), config 3 (one 32k-token
+         request on a random-init 36-layer W8A8 decoder, tokens/s/GPU) and config 4 (256
+         lognormal-length requests sharded over the ranks, tokens/s for the box).
 --impl reference: the reference's CPU path (the oracle's restatement of int8_quant
          quant_act + int_gemm_exact + dequant, numpy/float64 BLAS on all host threads) on a
          bounded sample: the four projections at M=256 per step.
@@ -281,6 +284,10 @@ def run_mica(args, rank, world, local):
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_total, e2e_ms, gemm_ms = t.tolist()
+    extra = {}
+    if not args.skip_model:
+        extra['config2_chain'] = run_chain(dev)
+        extra.update(run_prefill(dev, rank, world))
     if rank != 0:
         return None
     step_ops = OPS_PER_TOKEN * sum(MS)
@@ -309,8 +316,154 @@ def run_mica(args, rank, world, local):
                      'peak_source': f"2 x {pk['source']} bf16 dense ({pk['bf16']} TFLOP/s); nominal dense int8 4500",
                      'frac_of_nominal_4500': round(achieved / 4500.0, 4)},
         'clocks': clocks,
+        'other_configs': extra,
     }
     return line
+
+
+# ---------------------------------------------------------------------------------------
+def run_chain(dev, reps=20):
+    """RMSNorm + quant -> gate_up GEMM + SwiGLU + requant -> down GEMM at
+    M=4096 (x N(0,1) bf16 with 0.1% outliers x50 in 8 fixed channels, gamma N(1, 0.1))."""
+    import torch
+    from mica_b200 import _native as Nat
+    from mica_b200.int8_runtime import interleave_gate_up
+    M, H, I = 4096, 2560, 9728
+    g = torch.Generator(device=dev).manual_seed(2)
+    x = torch.randn(M, H, generator=g, device=dev)
+    ch = torch.randperm(H, generator=g, device=dev)[:8]
+    n_out = round(0.001 * M * H)
+    rows = torch.randint(0, M, (n_out,), generator=g, device=dev)
+    cols = ch[torch.randint(0, 8, (n_out,), generator=g, device=dev)]
+    x[rows, cols] *= 50
+    x = x.to(torch.bfloat16)
+    gamma = (1 + 0.1 * torch.randn(H, generator=g, device=dev)).to(torch.bfloat16)
+    wg = torch.randint(-127, 128, (I, H), generator=g, device=dev, dtype=torch.int8)
+    wu = torch.randint(-127, 128, (I, H), generator=g, device=dev, dtype=torch.int8)
+    sg = torch.rand(I, generator=g, device=dev) * 9e-3 + 1e-3
+    su = torch.rand(I, generator=g, device=dev) * 9e-3 + 1e-3
+    wgu, sgu = interleave_gate_up(wg, wu), interleave_gate_up(sg, su)
+    wd = torch.randint(-127, 128, (H, I), generator=g, device=dev, dtype=torch.int8)
+    sd = torch.rand(H, generator=g, device=dev) * 9e-3 + 1e-3
+
+    def chain():
+        q, s, _, _ = torch.ops.mica.rmsnorm_quant(x, None, gamma, None, 1e-6, Nat.NORM_WEIGHT, 0, False, True)
+        _, qh, sh = torch.ops.mica.gemm_swiglu_quant(q, s, wgu, sgu, None, 0)
+        return torch.ops.mica.w8a8_gemm(qh, sh, wd, sd, None, 0, 0)
+
+    us = _graph_time(dev, chain, reps)
+    ops = 2 * M * 2 * I * H + 2 * M * H * I
+    return {'config': 'config2: M=4096 RMSNorm+quant -> gate_up+SwiGLU+requant -> down', 'us_per_chain': round(us, 1),
+            'gemm_tops': round(ops / us / 1e6, 1), 'launches_per_chain': 3}
+
+
+def _graph_time(dev, fn, reps):
+    """Mean device time of fn() over `reps` replays of one graph holding [L2 flush, event,
+    fn, event] per rep (events bracket fn exactly; the flush evicts L2 between reps)."""
+    import torch
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    ev = [(torch.cuda.Event(enable_timing=True, external=True), torch.cuda.Event(enable_timing=True, external=True))
+          for _ in range(reps)]
+    s2 = torch.cuda.Stream(device=dev)
+    s2.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(s2):
+        for _ in range(3):
+            fn()
+    torch.cuda.current_stream(dev).wait_stream(s2)
+    g2 = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g2):
+        for a, b in ev:
+            flush.fill_(1)
+            a.record()
+            fn()
+            b.record()
+    g2.replay()
+    g2.replay()
+    torch.cuda.synchronize(dev)
+    t = sum(a.elapsed_time(b) for a, b in ev) / reps * 1e3
+    del g2
+    return t
+
+
+def request_set(seed=4, n=256):
+    """BASELINE config 4 load: lengths clip(round(exp(N(ln 1024, 1.0))), 256, 32768) (sigma
+    1.0 pinned here, BASELINE gives none) and 2-255 options each, seeded."""
+    import numpy as np
+    rng = np.random.default_rng(seed)
+    lengths = np.clip(np.round(np.exp(rng.normal(np.log(1024.0), 1.0, n))), 256, 32768).astype(int)
+    n_opts = rng.integers(2, 256, n)
+    ids = [rng.integers(0, 151936, int(L)) for L in lengths]
+    return lengths, n_opts, ids
+
+
+def shard(lengths, world, rank):
+    """Greedy longest-processing-time split by cost ~ L + L^2 / 8192 (linears + attention)."""
+    cost = [int(L) + int(L) * int(L) / 8192.0 for L in lengths]
+    order = sorted(range(len(lengths)), key=lambda i: -cost[i])
+    load = [0.0] * world
+    mine = []
+    for i in order:
+        r = min(range(world), key=lambda j: load[j])
+        load[r] += cost[i]
+        if r == rank:
+            mine.append(i)
+    return sorted(mine)
+
+
+def run_prefill(dev, rank, world, graph_max=2048):
+    """BASELINE configs 3 and 4 on a random-init 36-layer W8A8 decoder (4B dims, vocab 151936)."""
+    import torch
+    import torch.distributed as dist
+    from mica_b200 import prefill as P
+    cfg = P.DecoderConfig()
+    model = P.random_decoder(cfg, dev, seed=1)
+    gen = torch.Generator().manual_seed(9)
+    options = torch.randperm(cfg.vocab, generator=gen)[:257]        # No, Yes + 255 option labels
+    pf = P.Prefill(model, options, max_len=32768)
+    out = {}
+    # config 3: one 32768-token request, 255 options (rows 2..257 of the readout)
+    ids = torch.randint(0, cfg.vocab, (32768,), generator=gen).to(dev)
+    for _ in range(2):
+        pf.score(ids, 2, 257, graphs=False)
+    torch.cuda.synchronize(dev)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 3
+    a.record()
+    for _ in range(reps):
+        z, p = pf.score(ids, 2, 257, graphs=False)
+    b.record()
+    b.synchronize()
+    ms = a.elapsed_time(b) / reps
+    out['config3_32k'] = {'ms_per_request': round(ms, 2), 'tokens_per_s_per_gpu': round(32768 / ms * 1e3),
+                          'prob_sum': round(float(p.sum()), 6)}
+    # config 4: 256 requests sharded over the ranks, graphs for buckets up to graph_max
+    lengths, n_opts, req_ids = request_set()
+    mine = shard(lengths, world, rank)
+    for L in sorted({pf.bucket(int(lengths[i])) for i in mine if lengths[i] <= graph_max}):
+        pf.capture(L)
+    dev_ids = [torch.from_numpy(req_ids[i]).to(dev) for i in mine]
+    # warm-up pass over every request (as a server warms its shapes at start-up), then time
+    for j, i in enumerate(mine):
+        pf.score(dev_ids[j], 2, 2 + int(n_opts[i]))
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    a.record()
+    for j, i in enumerate(mine):
+        pf.score(dev_ids[j], 2, 2 + int(n_opts[i]))
+    b.record()
+    b.synchronize()
+    t = torch.tensor([a.elapsed_time(b)], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total = int(lengths.sum())
+    out['config4_batch256'] = {'requests': len(lengths), 'tokens': total, 'ms_box': round(float(t.item()), 1),
+                               'tokens_per_s_box': round(total / float(t.item()) * 1e3),
+                               'graph_buckets': len(pf.graphs), 'sharding': f'LPT over {world} ranks, no collective'}
+    pf.release()
+    del model, pf
+    torch.cuda.empty_cache()
+    return out
 
 
 def run_cpu_baseline(seconds=10.0):
@@ -384,6 +537,7 @@ def main():
     ap.add_argument('--cpu-seconds', type=float, default=10.0)
     ap.add_argument('--shape', default=None, help='M,N,K: time one linear shape only (profiling)')
     ap.add_argument('--tile', type=int, default=0, help='block_m*1000+block_n, 0 = library choice')
+    ap.add_argument('--skip-model', action='store_true', help='only the config-1 GEMM sweep')
     args = ap.parse_args()
     if args.shape:
         run_shape(args)

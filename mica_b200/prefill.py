@@ -33,7 +33,8 @@ from . import int8_kernels as K
 from . import ops  # noqa: F401
 from .int8_runtime import interleave_gate_up, quant_weight
 
-BUCKET = 64
+BUCKET = 64            # graph buckets (the reference's 64-token buckets)
+EAGER_BUCKET = 256     # padding granularity of eager (uncaptured) requests
 
 
 @dataclass
@@ -278,22 +279,35 @@ class Prefill:
         return torch.ops.mica.option_logits(h_last.contiguous(), self.rows, self.m.final_norm, lo, hi, self.cfg.eps,
                                             N.NORM_WEIGHT)
 
+    def eager_bucket(self, n: int) -> int:
+        """Padded length for an eager run: a multiple of EAGER_BUCKET, so request shapes (and
+        the attention library's per-shape plans) repeat across requests."""
+        return min(-(-n // EAGER_BUCKET) * EAGER_BUCKET, max(n, self.max_len))
+
     @torch.no_grad()
     def score(self, ids, lo=None, hi=None, graphs: bool = True):
         """ids: 1-D int64 tensor on the device; lo/hi: the option slice (ints, default all
-        rows). Uses a captured graph when the request's bucket has one, else runs eagerly.
-        Returns (logits, probs) fp32 [1, n_rows]."""
+        rows). Uses a captured graph when the request's bucket has one, else runs eagerly on
+        ids padded to a 256-token bucket (`limit` masks the padding). Returns (logits, probs)
+        fp32 [1, n_rows]."""
         n = int(ids.shape[0])
         if graphs and self.bucket(n) in self.graphs:
             return self.replay(ids, lo, hi)
         dev = ids.device
+        limit = None
+        L = self.eager_bucket(n)
+        if L != n:
+            padded = torch.zeros(L, dtype=ids.dtype, device=dev)
+            padded[:n].copy_(ids)
+            ids = padded
+            limit = torch.full((1,), n, dtype=torch.long, device=dev)
         lo_t = None if lo is None else torch.tensor([int(lo)], dtype=torch.int32, device=dev)
         hi_t = None if hi is None else torch.tensor([int(hi)], dtype=torch.int32, device=dev)
         if lo_t is not None and hi_t is None:
             hi_t = torch.tensor([self.rows.shape[0]], dtype=torch.int32, device=dev)
         if hi_t is not None and lo_t is None:
             lo_t = torch.zeros(1, dtype=torch.int32, device=dev)
-        return self.probs(self.hidden_last(ids), lo_t, hi_t)
+        return self.probs(self.hidden_last(ids, limit), lo_t, hi_t)
 
     # ---- CUDA graphs ------------------------------------------------------------------------
     def bucket(self, n: int) -> int:

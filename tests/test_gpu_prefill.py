@@ -124,3 +124,15 @@ def test_qk_norm_rope_matches_hf_torch_ops(S, H, KV):
         assert torch.allclose(got.float(), ref.float(), rtol=1e-2, atol=2e-2)
         assert float((got != ref).float().mean()) < 0.01
     assert torch.equal(qkv[:, (H + KV) * D:], v_before)
+
+
+def test_eager_padding_matches_unpadded_run(tiny):
+    """Eager requests are padded to a 256-token bucket with `limit`: same scores as the
+    unpadded computation (within attention-kernel rounding)."""
+    pf, g = tiny
+    ids = torch.from_numpy(g['m/ids1']).cuda()                 # 100 tokens -> padded to 256
+    z_pad, p_pad = (t.clone() for t in pf.score(ids, 0, 40, graphs=False))
+    z_raw, p_raw = pf.probs(pf.hidden_last(ids), torch.tensor([0], dtype=torch.int32, device='cuda'),
+                            torch.tensor([40], dtype=torch.int32, device='cuda'))
+    assert pf.eager_bucket(100) == 256
+    assert torch.allclose(p_pad, p_raw, atol=1e-3, rtol=0)
