@@ -503,9 +503,13 @@ def run_reference(args):
 
 
 def run_shape(args):
-    """One W8A8 linear shape (quantiser + GEMM), for profiler captures: prints ms and TOPS."""
+    """One kernel on one shape, for profiler captures (--kernel gemm | swiglu | act_quant |
+    rmsnorm_quant | readout): `--warmup` untimed launches, then `--steps` launches.
+    Prints the mean device time per launch (back-to-back launches, CUDA events)."""
     import torch
     import mica_b200.int8_kernels as K
+    from mica_b200 import _native as Nat
+    from mica_b200.int8_runtime import interleave_gate_up
     m, n, k = (int(v) for v in args.shape.split(','))
     dev = torch.device('cuda', 0)
     K.preload(dev)
@@ -514,18 +518,39 @@ def run_shape(args):
     w = torch.randint(-127, 128, (n, k), generator=g, device=dev, dtype=torch.int8)
     sw = torch.rand(n, generator=g, device=dev) * 9e-3 + 1e-3
     q, s = torch.ops.mica.act_quant(x, None, 0)
+    gamma = (1 + 0.1 * torch.randn(k, generator=g, device=dev)).to(torch.bfloat16)
+    if args.kernel == 'gemm':
+        fn, work = (lambda: torch.ops.mica.w8a8_gemm(q, s, w, sw, None, 0, args.tile)), ('TOPS', 2 * m * n * k)
+    elif args.kernel == 'swiglu':
+        wgu = interleave_gate_up(w[: n // 2], w[n // 2:])
+        sgu = interleave_gate_up(sw[: n // 2], sw[n // 2:])
+        fn, work = (lambda: torch.ops.mica.gemm_swiglu_quant(q, s, wgu, sgu, None, 0)), ('TOPS', 2 * m * n * k)
+    elif args.kernel == 'act_quant':
+        fn, work = (lambda: torch.ops.mica.act_quant(x, None, 0)), ('GB/s', m * k * 3 + 4 * m)
+    elif args.kernel == 'rmsnorm_quant':
+        r = torch.randn(m, k, generator=g, device=dev).to(torch.bfloat16)
+        fn = lambda: torch.ops.mica.rmsnorm_quant(x, r, gamma, None, 1e-6, Nat.NORM_WEIGHT, 0, False, True)  # noqa: E731
+        work = ('GB/s', m * k * (2 + 2 + 2 + 1) + 4 * m)
+    elif args.kernel == 'readout':
+        rows = torch.randn(n, k, generator=g, device=dev) * 0.02
+        hl = x[:m]
+        fn = lambda: torch.ops.mica.option_logits(hl, rows, gamma, None, None, 1e-6, Nat.NORM_WEIGHT)  # noqa: E731
+        work = ('GB/s', n * k * 4 + m * k * 2)
+    else:
+        raise SystemExit(f'unknown kernel {args.kernel}')
     for _ in range(args.warmup):
-        torch.ops.mica.w8a8_gemm(q, s, w, sw, None, 0, args.tile)
+        fn()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
     for _ in range(args.steps):
-        q, s = torch.ops.mica.act_quant(x, None, 0)
-        torch.ops.mica.w8a8_gemm(q, s, w, sw, None, 0, args.tile)
+        fn()
     b.record()
     torch.cuda.synchronize()
     ms = a.elapsed_time(b) / args.steps
-    print(json.dumps({'shape': [m, n, k], 'tile': args.tile, 'ms_per_linear': round(ms, 4),
-                      'tops_incl_quant': round(2 * m * n * k / ms / 1e9, 1)}), flush=True)
+    unit, amount = work
+    rate = amount / ms / 1e9 if unit == 'TOPS' else amount / ms / 1e6
+    print(json.dumps({'kernel': args.kernel, 'shape': [m, n, k], 'tile': args.tile, 'ms_per_launch': round(ms, 4),
+                      unit: round(rate, 1)}), flush=True)
 
 
 def main():
@@ -535,7 +560,8 @@ def main():
     ap.add_argument('--warmup', type=int, default=5)
     ap.add_argument('--impl', choices=('mica', 'reference'), default='mica')
     ap.add_argument('--cpu-seconds', type=float, default=10.0)
-    ap.add_argument('--shape', default=None, help='M,N,K: time one linear shape only (profiling)')
+    ap.add_argument('--shape', default=None, help='M,N,K: time one kernel on one shape (profiling)')
+    ap.add_argument('--kernel', default='gemm', help='gemm | swiglu | act_quant | rmsnorm_quant | readout')
     ap.add_argument('--tile', type=int, default=0, help='block_m*1000+block_n, 0 = library choice')
     ap.add_argument('--skip-model', action='store_true', help='only the config-1 GEMM sweep')
     args = ap.parse_args()

@@ -275,17 +275,27 @@ __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
+// ---- division by a per-row scale -----------------------------------------------------
+// RN(x / s) given r = RN(1 / s) (one __frcp_rn per row). Markstein's theorem: when r is the
+// correctly rounded reciprocal, q0 = RN(x * r) is within one ulp of x / s, the residual
+// x - q0 * s is exact in one FMA, and RN(q0 + residual * r) equals RN(x / s) -- for every
+// quotient in the normal range. Smaller quotients (|x / s| < 2^-126) quantise to 0 under
+// either rounding mode, so the codes are those of the IEEE division. Three instructions,
+// no slow-path branch, unlike a full division per element.
+__device__ __forceinline__ float div_by_scale(float x, float s, float r) {
+    const float q0 = __fmul_rn(x, r);
+    const float e = __fmaf_rn(-q0, s, x);
+    return __fmaf_rn(e, r, q0);
+}
+
 // ---- rounding shared by the quantisers ---------------------------------------------
 // v = x / scale in IEEE fp32. HALF_AWAY follows the reference GPU kernel literally:
 // add +-0.5 in fp32 (so the sum itself is rounded) and truncate toward zero.
+// copysign(0.5, v) equals the reference's (v >= 0 ? +0.5 : -0.5) for every v that matters:
+// only -0.0 differs, and -0.0 - 0.5 = -0.5 truncates to the same 0.
 __device__ __forceinline__ int quant_round(float v, int round_mode) {
-    int r;
-    if (round_mode == MICA_ROUND_HALF_EVEN) {
-        r = __float2int_rn(v);
-    } else {
-        const float t = v >= 0.f ? __fadd_rn(v, 0.5f) : __fsub_rn(v, 0.5f);
-        r = __float2int_rz(t);
-    }
+    const int r = round_mode == MICA_ROUND_HALF_EVEN ? __float2int_rn(v)
+                                                      : __float2int_rz(__fadd_rn(v, copysignf(0.5f, v)));
     return min(max(r, -127), 127);
 }
 

@@ -411,6 +411,7 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
         for (int row = blockIdx.x * (blockDim.x >> 5) + warp; row < M; row += warps_total) {
             const unsigned bits = __ldcg(args.row_amax + row);
             const float scale = __fdiv_rn(fmaxf(__uint_as_float(bits), 1e-8f), 127.0f);
+            const float rscale = __frcp_rn(scale);
             const __nv_bfloat16* hrow = args.h + static_cast<long>(row) * args.ldh;
             int8_t* qrow = args.q_out + static_cast<long>(row) * args.ldq;
             // two 8-element vectors per lane per step: 16 independent divisions in flight
@@ -425,7 +426,7 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
                 for (int e = 0; e < 16; ++e) {
                     const uint32_t half = (w8[e >> 1] >> ((e & 1) * 16)) & 0xFFFFu;
                     const float x = __uint_as_float(half << 16);
-                    const int qv = quant_round(__fdiv_rn(x, scale), args.round_mode);
+                    const int qv = quant_round(div_by_scale(x, scale, rscale), args.round_mode);
                     out[e >> 2] |= (static_cast<uint32_t>(qv) & 0xFFu) << ((e & 3) * 8);
                 }
                 *reinterpret_cast<uint2*>(qrow + c) = make_uint2(out[0], out[1]);

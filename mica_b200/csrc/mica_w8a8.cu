@@ -322,16 +322,23 @@ static int quant_launch(const QuantArgs& a, int dtype, bool norm, cudaStream_t s
     if (threads < 32) threads = 32;
     if (threads > 1024) return MICA_ERR_UNSUPPORTED;
     const dim3 grid(a.M), block(threads);
-    if (dtype == MICA_DT_BF16) {
-        if (norm) quant_rows_kernel<__nv_bfloat16, true><<<grid, block, 0, st>>>(a);
-        else quant_rows_kernel<__nv_bfloat16, false><<<grid, block, 0, st>>>(a);
-    } else if (dtype == MICA_DT_FP16) {
-        if (norm) quant_rows_kernel<__half, true><<<grid, block, 0, st>>>(a);
-        else quant_rows_kernel<__half, false><<<grid, block, 0, st>>>(a);
-    } else {
-        if (norm) return MICA_ERR_ARG;
-        quant_rows_kernel<float, false><<<grid, block, 0, st>>>(a);
+    if (norm && dtype == MICA_DT_FP32) return MICA_ERR_ARG;
+#define QLAUNCH(MAXT)                                                                         \
+    if (dtype == MICA_DT_BF16) {                                                              \
+        if (norm) quant_rows_kernel<__nv_bfloat16, true, MAXT><<<grid, block, 0, st>>>(a);    \
+        else quant_rows_kernel<__nv_bfloat16, false, MAXT><<<grid, block, 0, st>>>(a);       \
+    } else if (dtype == MICA_DT_FP16) {                                                       \
+        if (norm) quant_rows_kernel<__half, true, MAXT><<<grid, block, 0, st>>>(a);           \
+        else quant_rows_kernel<__half, false, MAXT><<<grid, block, 0, st>>>(a);              \
+    } else {                                                                                  \
+        quant_rows_kernel<float, false, MAXT><<<grid, block, 0, st>>>(a);                     \
     }
+    if (threads <= 512) {
+        QLAUNCH(512)
+    } else {
+        QLAUNCH(1024)
+    }
+#undef QLAUNCH
     return launch_status();
 }
 

@@ -100,9 +100,10 @@ struct QuantArgs {
     int M, K, round_mode;
 };
 
-// NORM = false: mica_act_quant. NORM = true: mica_rmsnorm_quant.
-template <typename T, bool NORM>
-__global__ void __launch_bounds__(1024) quant_rows_kernel(const QuantArgs a) {
+// NORM = false: mica_act_quant. NORM = true: mica_rmsnorm_quant. MAXT bounds the block
+// size (512 for rows up to 16384 elements, 1024 beyond), which bounds registers per thread.
+template <typename T, bool NORM, int MAXT = 512>
+__global__ void __launch_bounds__(MAXT) quant_rows_kernel(const QuantArgs a) {
     __shared__ float red[32];
     const int row = blockIdx.x;
     const int nvec = a.K >> 3;
@@ -182,6 +183,7 @@ __global__ void __launch_bounds__(1024) quant_rows_kernel(const QuantArgs a) {
         for (int e = 0; e < 8; ++e) am = fmaxf(am, fabsf(v[i][e]));
     am = block_reduce<true>(am, red);
     const float scale = __fdiv_rn(fmaxf(am, 1e-8f), 127.0f);
+    const float rscale = __frcp_rn(scale);
     int8_t* qr = a.q + static_cast<long>(row) * a.ldq;
 #pragma unroll
     for (int i = 0; i < QV; ++i) {
@@ -190,7 +192,7 @@ __global__ void __launch_bounds__(1024) quant_rows_kernel(const QuantArgs a) {
             uint32_t o[2] = {0u, 0u};
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
-                const int qv = quant_round(__fdiv_rn(v[i][e], scale), a.round_mode);
+                const int qv = quant_round(div_by_scale(v[i][e], scale, rscale), a.round_mode);
                 o[e >> 2] |= (static_cast<uint32_t>(qv) & 0xFFu) << ((e & 3) * 8);
             }
             *reinterpret_cast<uint2*>(qr + idx * 8) = make_uint2(o[0], o[1]);
