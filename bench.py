@@ -88,6 +88,30 @@ def cpu_sample(O, rows=256, reps=1, seed=0):
     return ops, time.perf_counter() - t0
 
 
+def host_cores():
+    try:
+        return len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
+
+
+class all_host_threads:
+    """BLAS on every host core, whatever OMP_NUM_THREADS the launcher set (torchrun sets 1)."""
+
+    def __enter__(self):
+        self.n = host_cores()
+        try:
+            from threadpoolctl import threadpool_limits
+            self.ctx = threadpool_limits(limits=self.n)
+        except Exception:
+            self.ctx = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.ctx is not None:
+            self.ctx.restore_original_limits()
+
+
 def cpu_threads():
     try:
         import threadpoolctl
@@ -97,7 +121,7 @@ def cpu_threads():
             return max(blas)
     except Exception:
         pass
-    return os.cpu_count() or 1
+    return host_cores()
 
 
 # ---------------------------------------------------------------------------------------
@@ -468,29 +492,32 @@ def run_prefill(dev, rank, world, graph_max=2048):
 
 def run_cpu_baseline(seconds=10.0):
     O = load_oracle()
-    cpu_sample(O, rows=32)  # warm
-    ops, secs, reps = 0, 0.0, 0
-    while secs < seconds and reps < 50:
-        o, s = cpu_sample(O, rows=256, seed=reps)
-        ops += o
-        secs += s
-        reps += 1
-    return {'value': round(ops / secs / 1e12, 4), 'unit': UNIT, 'cores': cpu_threads(), 'kind': 'port',
+    with all_host_threads():
+        cpu_sample(O, rows=32)  # warm
+        ops, secs, reps = 0, 0.0, 0
+        while secs < seconds and reps < 50:
+            o, s = cpu_sample(O, rows=256, seed=reps)
+            ops += o
+            secs += s
+            reps += 1
+        cores = cpu_threads()
+    return {'value': round(ops / secs / 1e12, 4), 'unit': UNIT, 'cores': cores, 'kind': 'port',
             'sample': f'{reps} x (4 projections at M=256: quantise + exact int GEMM + dequant), {secs:.1f} s'}
 
 
 def run_reference(args):
     O = load_oracle()
-    cpu_sample(O, rows=32)
-    for i in range(args.warmup):
-        cpu_sample(O, rows=256, seed=100 + i)
-    ops, secs = 0, 0.0
-    for i in range(args.steps):
-        o, s = cpu_sample(O, rows=256, seed=i)
-        ops += o
-        secs += s
+    with all_host_threads():
+        cpu_sample(O, rows=32)
+        for i in range(args.warmup):
+            cpu_sample(O, rows=256, seed=100 + i)
+        ops, secs = 0, 0.0
+        for i in range(args.steps):
+            o, s = cpu_sample(O, rows=256, seed=i)
+            ops += o
+            secs += s
+        cores = cpu_threads()
     v = ops / secs / 1e12
-    cores = cpu_threads()
     return {
         'impl': 'reference', 'metric': METRIC, 'value': round(v, 4), 'unit': UNIT, 'n_gpus': args.gpus,
         'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': round(secs / args.steps * 1e3, 2),
@@ -586,7 +613,8 @@ def main():
     try:
         line = run_mica(args, rank, world, local)
         if rank == 0:
-            line['cpu_baseline'] = run_cpu_baseline(args.cpu_seconds)
+            if world == 1:      # the CPU baseline is reported at N=1 only
+                line['cpu_baseline'] = run_cpu_baseline(args.cpu_seconds)
             print(json.dumps(line), flush=True)
     finally:
         if world > 1:

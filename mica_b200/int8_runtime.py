@@ -278,3 +278,82 @@ def convert(body, stats, backend='aot', alpha=ALPHA, keep_bf16=False, fuse_mlp=F
         smoothed += smooth is not None
         del child
     return (replaced, smoothed)
+
+
+# ---------------------------------------------------------------------------------------
+# Start-up self-test, the reference's int8_runtime.selftest (lib/int8_runtime.py:362-443):
+# random weights per (N, K, bias) shape, a smoothed and an unsmoothed QLinear, the reference
+# rows; the kernels' output must be within 1.05x the INT8 emulation noise of the bf16
+# product, and every call must launch the library's kernels (2 per linear).
+SELFTEST_ROWS = (3, 48, 200, 608, 1500)
+SELFTEST_TOL = 1.05
+SELFTEST_SEED = 20261022
+
+
+def _row_rel(a, b):
+    return float(((a - b).norm(dim=-1) / b.norm(dim=-1).clamp_min(1e-30)).max())
+
+
+def selftest(shapes, device, rows=SELFTEST_ROWS):
+    """Returns {'ok', 'reason', 'checked', 'worst_ratio', 'launches', 'seconds'} like the
+    reference. The INT8 emulation runs on the device with exact float64 integer products."""
+    import time
+    import types
+
+    t0 = time.perf_counter()
+    out = {'ok': False, 'reason': '', 'checked': 0, 'worst_ratio': 0.0}
+    try:
+        dev = torch.device(device)
+        ok, why = aot.available(dev)
+        if not ok:
+            out['reason'] = why
+            return out
+        launches = aot.STATS['launch']
+        g = torch.Generator().manual_seed(SELFTEST_SEED)
+        for n, k, has_bias in shapes:
+            n, k = int(n), int(k)
+            w = (torch.randn(n, k, generator=g) * 0.05).to(torch.bfloat16)
+            amax = torch.rand(k, generator=g) * 4 + 0.05
+            amax[::61] *= 25.0
+            b = (torch.randn(n, generator=g) * 0.1).to(torch.bfloat16).to(dev) if has_bias else None
+            lin = types.SimpleNamespace(weight=w.to(dev), bias=b)
+            for smooth in (smooth_factors(amax, w, ALPHA), None):
+                q = QLinear(lin, smooth)
+                wd = q.qweight.float() * q.wscale[:, None]
+                if q.inv_smooth is not None:
+                    wd = wd * q.inv_smooth[None, :]
+                for m in rows:
+                    x = (torch.randn(m, k, generator=g) * amax / 3).to(torch.bfloat16).to(dev)
+                    l0 = aot.STATS['launch']
+                    y = q(x).float()
+                    if aot.STATS['launch'] - l0 < 2:
+                        out['reason'] = 'N %d K %d M %d: %d kernel launches (expected 2)' % (
+                            n, k, m, aot.STATS['launch'] - l0)
+                        return out
+                    ref = x.float() @ wd.t()
+                    xf = x.float() * q.inv_smooth if q.inv_smooth is not None else x.float()
+                    sx = xf.abs().amax(-1).clamp_min(EPS) / 127.0
+                    qx = torch.round(xf / sx[:, None]).clamp(-127, 127)
+                    acc = (qx.double() @ q.qweight.double().t()).round()
+                    emu = acc.float() * sx[:, None] * q.wscale[None, :]
+                    if q.bias is not None:
+                        ref, emu = ref + q.bias, emu + q.bias
+                    emu = emu.to(q.out_dtype).float()
+                    noise, err = _row_rel(emu, ref), _row_rel(y, ref)
+                    if not bool(torch.isfinite(y).all()):
+                        out['reason'] = 'non-finite output (N %d, K %d, M %d)' % (n, k, m)
+                        return out
+                    if not err <= SELFTEST_TOL * noise:
+                        out['reason'] = 'N %d K %d M %d: error %.4g > %.2f x INT8 noise %.4g' % (
+                            n, k, m, err, SELFTEST_TOL, noise)
+                        return out
+                    out['worst_ratio'] = max(out['worst_ratio'], err / max(noise, 1e-30))
+                    out['checked'] += 1
+        torch.cuda.synchronize(dev)
+        out.update(ok=True, reason='ok', launches=aot.STATS['launch'] - launches,
+                   worst_ratio=round(out['worst_ratio'], 5))
+    except Exception as exc:  # the reference reports, never raises
+        out['reason'] = ('%s: %s' % (type(exc).__name__, exc))[:300]
+    finally:
+        out['seconds'] = round(time.perf_counter() - t0, 2)
+    return out

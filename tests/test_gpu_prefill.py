@@ -136,3 +136,11 @@ def test_eager_padding_matches_unpadded_run(tiny):
                             torch.tensor([40], dtype=torch.int32, device='cuda'))
     assert pf.eager_bucket(100) == 256
     assert torch.allclose(p_pad, p_raw, atol=1e-3, rtol=0)
+
+
+def test_startup_selftest_like_the_reference():
+    from mica_b200 import int8_runtime as rt
+    res = rt.selftest([(6144, 2560, False), (2560, 4096, True), (2560, 9728, False)], 'cuda')
+    assert res['ok'], res
+    assert res['checked'] == 3 * 2 * len(rt.SELFTEST_ROWS)
+    assert res['worst_ratio'] <= rt.SELFTEST_TOL
