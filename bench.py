@@ -20,9 +20,9 @@ roofline: the GEMM kernel alone (per-launch CUDA events, averaged over the sweep
 other_configs: BASELINE config 2 (fused MLP chain, us per chain), config 3 (one 32k-token
          request on a random-init 36-layer W8A8 decoder, tokens/s/GPU) and config 4 (256
          lognormal-length requests sharded over the ranks, tokens/s for the box).
---impl reference: the reference's CPU path (the oracle's restatement of int8_quant
-         quant_act + int_gemm_exact + dequant, numpy/float64 BLAS on all host threads) on a
-         bounded sample: the four projections at M=256 per step.
+--impl reference: the reference's CPU path (the plain-C oracle's restatement of int8_quant
+         quant_act + exact int8 GEMM + dequant on every host core; numpy float64 if the C
+         oracle is not built) on a bounded sample: the four projections at M=256 per step.
 """
 from __future__ import annotations
 
@@ -50,12 +50,27 @@ CONFIG = {'workload': 'config1: 4B decoder-layer projection sweep (QKV/O/gate_up
           'parallelism': 'data-parallel replicas, no collective'}
 
 
-def load_oracle():
+def load_oracle(name='mica_oracle'):
     import importlib.util
-    spec = importlib.util.spec_from_file_location('mica_oracle', ROOT / 'oracle' / 'mica_oracle.py')
+    spec = importlib.util.spec_from_file_location(name, ROOT / 'oracle' / f'{name}.py')
     mod = importlib.util.module_from_spec(spec)
     spec.loader.exec_module(mod)
     return mod
+
+
+def cpu_path():
+    """The CPU implementation of the reference path timed here: the plain-C oracle (exact int8
+    GEMM with int32 accumulation on every host core, like the reference's torch int8 CPU
+    path) when built, else the numpy restatement (float64 BLAS, the reference's 'emulate')."""
+    O = load_oracle()
+    try:
+        C = load_oracle('oracle_c')
+        if C.available():
+            C.set_threads(host_cores())
+            return 'c', O, C
+    except OSError:
+        pass
+    return 'numpy', O, None
 
 
 def peaks():
@@ -67,10 +82,11 @@ def peaks():
 
 
 # ---------------------------------------------------------------------------------------
-def cpu_sample(O, rows=256, reps=1, seed=0):
+def cpu_sample(path, rows=256, reps=1, seed=0):
     """The reference's CPU path on a bounded sample: quantise + exact int GEMM + dequant
     for the four projections at `rows` tokens. Returns (ops, seconds)."""
     import numpy as np
+    kind, O, C = path
     rng = np.random.default_rng(seed)
     data = []
     for _, n, k in PROJECTIONS:
@@ -82,8 +98,12 @@ def cpu_sample(O, rows=256, reps=1, seed=0):
     t0 = time.perf_counter()
     for _ in range(reps):
         for x, qw, sw in data:
-            qx, sx = O.quant_act_half_even(x)
-            O.dequant_out(O.int_gemm_exact(qx, qw), sx, sw)
+            if C is not None:
+                qx, sx = C.quant_act(x, None, 'half_even')
+                C.dequant_bf16_bits(C.int_gemm(qx, qw), sx, sw)
+            else:
+                qx, sx = O.quant_act_half_even(x)
+                O.dequant_out(O.int_gemm_exact(qx, qw), sx, sw)
             ops += 2 * rows * qw.shape[0] * qw.shape[1]
     return ops, time.perf_counter() - t0
 
@@ -491,40 +511,43 @@ def run_prefill(dev, rank, world, graph_max=2048):
 
 
 def run_cpu_baseline(seconds=10.0):
-    O = load_oracle()
     with all_host_threads():
-        cpu_sample(O, rows=32)  # warm
+        path = cpu_path()
+        cpu_sample(path, rows=32)  # warm
         ops, secs, reps = 0, 0.0, 0
-        while secs < seconds and reps < 50:
-            o, s = cpu_sample(O, rows=256, seed=reps)
+        while secs < seconds and reps < 200:
+            o, s = cpu_sample(path, rows=256, seed=reps)
             ops += o
             secs += s
             reps += 1
-        cores = cpu_threads()
+        cores = path[2].threads() if path[2] is not None else cpu_threads()
     return {'value': round(ops / secs / 1e12, 4), 'unit': UNIT, 'cores': cores, 'kind': 'port',
-            'sample': f'{reps} x (4 projections at M=256: quantise + exact int GEMM + dequant), {secs:.1f} s'}
+            'sample': f'{reps} x (4 projections at M=256: quantise + exact int GEMM + dequant, '
+                      f'{path[0]} oracle), {secs:.1f} s of compute'}
 
 
 def run_reference(args):
-    O = load_oracle()
     with all_host_threads():
-        cpu_sample(O, rows=32)
+        path = cpu_path()
+        cpu_sample(path, rows=32)
         for i in range(args.warmup):
-            cpu_sample(O, rows=256, seed=100 + i)
+            cpu_sample(path, rows=256, seed=100 + i)
         ops, secs = 0, 0.0
         for i in range(args.steps):
-            o, s = cpu_sample(O, rows=256, seed=i)
+            o, s = cpu_sample(path, rows=256, seed=i)
             ops += o
             secs += s
-        cores = cpu_threads()
+        cores = path[2].threads() if path[2] is not None else cpu_threads()
     v = ops / secs / 1e12
     return {
         'impl': 'reference', 'metric': METRIC, 'value': round(v, 4), 'unit': UNIT, 'n_gpus': args.gpus,
         'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': round(secs / args.steps * 1e3, 2),
-        'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None, 'dtype': 'int8 x int8 -> int32 (fp64 BLAS)',
+        'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None,
+        'dtype': 'int8 x int8 -> int32' + (' (C, AVX2 int16 multiply-add)' if path[0] == 'c' else ' (float64 BLAS)'),
         'data': 'synthetic (seeded)', 'config': CONFIG,
         'cpu_baseline': {'value': round(v, 4), 'unit': UNIT, 'cores': cores, 'kind': 'port',
-                         'sample': 'per step: the 4 projections at M=256 (quantise + exact int GEMM + dequant)'},
+                         'sample': f'per step: the 4 projections at M=256 (quantise + exact int GEMM + dequant, '
+                                   f'{path[0]} oracle)'},
         'e2e': {'value': round(v, 4), 'unit': UNIT, 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0},
     }
 

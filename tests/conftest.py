@@ -23,6 +23,16 @@ def _load_oracle():
 ORACLE = _load_oracle()
 
 
+def _load_oracle_c():
+    spec = importlib.util.spec_from_file_location('mica_oracle_c', ROOT / 'oracle' / 'oracle_c.py')
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+ORACLE_C = _load_oracle_c()
+
+
 @lru_cache(maxsize=None)
 def golden(name):
     return np.load(GOLDEN / f'{name}.npz')
