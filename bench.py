@@ -454,7 +454,23 @@ def shard(lengths, world, rank):
     return sorted(mine)
 
 
-def run_prefill(dev, rank, world, graph_max=2048):
+def plan_batches(lengths, batch_tokens):
+    """Groups request indices by sorted length so that (count x 64-token bucket of the
+    longest) stays within batch_tokens; a longer request goes alone."""
+    order = sorted(range(len(lengths)), key=lambda i: lengths[i])
+    out, cur = [], []
+    for i in order:
+        L = -(-lengths[i] // 64) * 64
+        if cur and (len(cur) + 1) * L > batch_tokens:
+            out.append(cur)
+            cur = []
+        cur.append(i)
+    if cur:
+        out.append(cur)
+    return out
+
+
+def run_prefill(dev, rank, world, batch_tokens=16384):
     """BASELINE configs 3 and 4 on a random-init 36-layer W8A8 decoder (4B dims, vocab 151936)."""
     import torch
     import torch.distributed as dist
@@ -480,21 +496,24 @@ def run_prefill(dev, rank, world, graph_max=2048):
     ms = a.elapsed_time(b) / reps
     out['config3_32k'] = {'ms_per_request': round(ms, 2), 'tokens_per_s_per_gpu': round(32768 / ms * 1e3),
                           'prob_sum': round(float(p.sum()), 6)}
-    # config 4: 256 requests sharded over the ranks, graphs for buckets up to graph_max
+    # config 4: 256 requests sharded over the ranks; each rank scores its share in batches of
+    # similar length (sorted, padded to 64-token buckets, up to batch_tokens rows per pass)
     lengths, n_opts, req_ids = request_set()
     mine = shard(lengths, world, rank)
-    for L in sorted({pf.bucket(int(lengths[i])) for i in mine if lengths[i] <= graph_max}):
-        pf.capture(L)
-    dev_ids = [torch.from_numpy(req_ids[i]).to(dev) for i in mine]
-    # warm-up pass over every request (as a server warms its shapes at start-up), then time
-    for j, i in enumerate(mine):
-        pf.score(dev_ids[j], 2, 2 + int(n_opts[i]))
+    batches = plan_batches([int(lengths[i]) for i in mine], batch_tokens)
+    dev_ids = {i: torch.from_numpy(req_ids[i]).to(dev) for i in mine}
+
+    def run_batches():
+        for bt in batches:
+            reqs = [mine[j] for j in bt]
+            pf.score_batch([dev_ids[i] for i in reqs], [(2, 2 + int(n_opts[i])) for i in reqs])
+
+    run_batches()         # warm-up pass over every batch shape (as a server warms up at start)
     torch.cuda.synchronize(dev)
     if world > 1:
         dist.barrier()
     a.record()
-    for j, i in enumerate(mine):
-        pf.score(dev_ids[j], 2, 2 + int(n_opts[i]))
+    run_batches()
     b.record()
     b.synchronize()
     t = torch.tensor([a.elapsed_time(b)], device=dev, dtype=torch.float64)
@@ -503,7 +522,8 @@ def run_prefill(dev, rank, world, graph_max=2048):
     total = int(lengths.sum())
     out['config4_batch256'] = {'requests': len(lengths), 'tokens': total, 'ms_box': round(float(t.item()), 1),
                                'tokens_per_s_box': round(total / float(t.item()) * 1e3),
-                               'graph_buckets': len(pf.graphs), 'sharding': f'LPT over {world} ranks, no collective'}
+                               'batches_rank0': len(batches), 'batch_tokens': batch_tokens,
+                               'sharding': f'LPT over {world} ranks, no collective'}
     pf.release()
     del model, pf
     torch.cuda.empty_cache()
@@ -581,6 +601,13 @@ def run_shape(args):
         r = torch.randn(m, k, generator=g, device=dev).to(torch.bfloat16)
         fn = lambda: torch.ops.mica.rmsnorm_quant(x, r, gamma, None, 1e-6, Nat.NORM_WEIGHT, 0, False, True)  # noqa: E731
         work = ('GB/s', m * k * (2 + 2 + 2 + 1) + 4 * m)
+    elif args.kernel == 'qk_rope':
+        from mica_b200 import prefill as P
+        qkv = torch.randn(m, 6144, generator=g, device=dev).to(torch.bfloat16)
+        cos, sin = P.rope_tables(P.DecoderConfig(), m, dev)
+        qw = gamma[:128].contiguous()
+        fn = lambda: torch.ops.mica.qk_norm_rope(qkv, qw, qw, cos, sin, None, 0, 32, 8, 1e-6)  # noqa: E731
+        work = ('GB/s', m * 5120 * 2 * 2)
     elif args.kernel == 'readout':
         rows = torch.randn(n, k, generator=g, device=dev) * 0.02
         hl = x[:m]
@@ -611,7 +638,7 @@ def main():
     ap.add_argument('--impl', choices=('mica', 'reference'), default='mica')
     ap.add_argument('--cpu-seconds', type=float, default=10.0)
     ap.add_argument('--shape', default=None, help='M,N,K: time one kernel on one shape (profiling)')
-    ap.add_argument('--kernel', default='gemm', help='gemm | swiglu | act_quant | rmsnorm_quant | readout')
+    ap.add_argument('--kernel', default='gemm', help='gemm | swiglu | act_quant | rmsnorm_quant | qk_rope | readout')
     ap.add_argument('--tile', type=int, default=0, help='block_m*1000+block_n, 0 = library choice')
     ap.add_argument('--skip-model', action='store_true', help='only the config-1 GEMM sweep')
     args = ap.parse_args()

@@ -181,6 +181,7 @@ class Prefill:
         self.scale = cfg.head_dim ** -0.5
         self.graphs = {}
         self.pool = None
+        self._pos = {}
         if attn_backends is None:
             from torch.nn.attention import SDPBackend
             attn_backends = [SDPBackend.CUDNN_ATTENTION, SDPBackend.FLASH_ATTENTION, SDPBackend.EFFICIENT_ATTENTION]
@@ -196,78 +197,84 @@ class Prefill:
         return torch.ops.mica.w8a8_gemm(q, s, w, sw, None, 0, K.tiles.tile(w.shape[0], w.shape[1], q.shape[0]))
 
     def _attention(self, q, k, v, causal, mask=None):
+        """q [B, Sq, H, D], k/v [B, Sk, KV, D] (strided views are fine) -> [B*Sq, H*D]."""
         from torch.nn.attention import sdpa_kernel
-        qh, kh, vh = q.transpose(0, 1)[None], k.transpose(0, 1)[None], v.transpose(0, 1)[None]
         with sdpa_kernel(self.backends):
-            o = F.scaled_dot_product_attention(qh, kh, vh, attn_mask=mask, is_causal=causal and mask is None,
-                                               scale=self.scale, enable_gqa=True)
-        return o[0].transpose(0, 1).reshape(q.shape[0], -1).contiguous()
+            o = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2),
+                                               attn_mask=mask, is_causal=causal and mask is None, scale=self.scale,
+                                               enable_gqa=True)
+        return o.transpose(1, 2).reshape(q.shape[0] * q.shape[1], -1).contiguous()
 
     def _mlp(self, q, s, lay):
         _, qh, sh = torch.ops.mica.gemm_swiglu_quant(q, s, lay.gu_w, lay.gu_s, None, K._round_code())
         return self._gemm(qh, sh, lay.down_w, lay.down_s)
 
+    def _positions(self, B, L, device):
+        """Row positions of a [B, L] batch (None for B = 1: the kernel uses the row index)."""
+        if B == 1:
+            return None
+        key = (B, L)
+        if key not in self._pos:
+            self._pos[key] = torch.arange(L, device=device, dtype=torch.long).repeat(B)
+        return self._pos[key]
+
     # ---- forward -------------------------------------------------------------------------
     def hidden_last(self, ids: torch.Tensor, limit: torch.Tensor = None, last_only: bool = True):
-        """Runs the decoder over ids [S] and returns the last real row's hidden state
-        (before the final norm) as bf16 [1, hidden]. `limit` (int tensor [1]) marks the real
-        length when ids are padded to a bucket; keys at or past it are masked."""
+        """Runs the decoder over ids [S] (one request) or [B, L] (B requests padded to L) and
+        returns each request's last real row's hidden state (before the final norm) as bf16
+        [B, hidden]. `limit` (int64 [B]) is each request's real length when padded; keys at
+        or past it are masked for the scored row, and no real row attends to later rows."""
         cfg, m = self.cfg, self.m
-        S = ids.shape[0]
-        cos, sin = self.cos[:S], self.sin[:S]
-        h = F.embedding(ids, m.embed)
+        if ids.dim() == 1:
+            ids = ids[None]
+        B, L = ids.shape
+        M = B * L
+        pos = self._positions(B, L, ids.device)
+        h = F.embedding(ids.reshape(-1), m.embed)
         prev = None
         nl = len(m.layers)
         for li, lay in enumerate(m.layers):
             q8, s8, h = self._norm_quant(prev if prev is not None else h, lay.in_norm,
                                          h if prev is not None else None)
             if li == nl - 1 and last_only:
-                return self._last_layer(q8, s8, h, lay, cos, sin, limit)
+                return self._last_layer(q8, s8, h, lay, B, L, pos, limit)
             qkv = self._gemm(q8, s8, lay.qkv_w, lay.qkv_s)
-            torch.ops.mica.qk_norm_rope(qkv, lay.q_norm, lay.k_norm, self.cos, self.sin, None, 0, cfg.heads,
+            torch.ops.mica.qk_norm_rope(qkv, lay.q_norm, lay.k_norm, self.cos, self.sin, pos, 0, cfg.heads,
                                         cfg.kv_heads, cfg.eps)
             q, k, v = qkv.split([cfg.q_dim, cfg.kv_dim, cfg.kv_dim], dim=1)
-            attn = self._attention(q.view(S, cfg.heads, cfg.head_dim), k.view(S, cfg.kv_heads, cfg.head_dim),
-                                   v.view(S, cfg.kv_heads, cfg.head_dim), causal=True)
+            attn = self._attention(q.view(B, L, cfg.heads, cfg.head_dim), k.view(B, L, cfg.kv_heads, cfg.head_dim),
+                                   v.view(B, L, cfg.kv_heads, cfg.head_dim), causal=True)
             qa, sa = torch.ops.mica.act_quant(attn, None, K._round_code())
             o = self._gemm(qa, sa, lay.o_w, lay.o_s)
             q8, s8, h = self._norm_quant(o, lay.post_norm, h)
             prev = self._mlp(q8, s8, lay)
-        # full path: pick the last real row after the final residual add
-        out = (h + prev)
-        return self._pick(out, limit)
+        out = h + prev
+        return out.index_select(0, self._scored_rows(B, L, limit, out.device))
 
-    def _pick(self, t, limit):
-        if limit is None:
-            return t[-1:]
-        idx = (limit - 1).view(1, 1).expand(1, t.shape[1])
-        return t.gather(0, idx)
+    def _scored_rows(self, B, L, limit, device):
+        base = torch.arange(B, device=device, dtype=torch.long) * L
+        return base + ((limit.view(B) - 1) if limit is not None else L - 1)
 
-    def _last_layer(self, q8, s8, h, lay, cos, sin, limit):
-        """K/V for every row, Q / attention / O / MLP for the scored row only."""
+    def _last_layer(self, q8, s8, h, lay, B, L, pos, limit):
+        """K/V for every row, Q / attention / O / MLP for each request's scored row only."""
         cfg = self.cfg
-        S = q8.shape[0]
         qd, kd = cfg.q_dim, cfg.kv_dim
+        dev = q8.device
         kv = self._gemm(q8, s8, lay.qkv_w[qd:], lay.qkv_s[qd:])
-        torch.ops.mica.qk_norm_rope(kv, None, lay.k_norm, self.cos, self.sin, None, 0, 0, cfg.kv_heads, cfg.eps)
+        torch.ops.mica.qk_norm_rope(kv, None, lay.k_norm, self.cos, self.sin, pos, 0, 0, cfg.kv_heads, cfg.eps)
         k, v = kv.split([kd, kd], dim=1)
-        if limit is None:
-            row_q8, row_s8, res = q8[-1:], s8[-1:], h[-1:]
-            pos = torch.full((1,), S - 1, dtype=torch.long, device=q8.device)
-            mask = None
-        else:
-            li = (limit - 1).view(1)
-            row_q8 = q8.index_select(0, li)
-            row_s8 = s8.index_select(0, li)
-            res = h.index_select(0, li)
-            pos = li.to(torch.long)
-            keys = torch.arange(S, device=q8.device)
-            mask = torch.where(keys[None, :] < limit.view(1, 1), 0.0, float('-inf')).to(torch.bfloat16)
-            mask = mask.view(1, 1, 1, S)
+        rows = self._scored_rows(B, L, limit, dev)
+        row_q8, row_s8, res = q8.index_select(0, rows), s8.index_select(0, rows), h.index_select(0, rows)
+        qpos = (limit.view(B) - 1) if limit is not None else torch.full((B,), L - 1, dtype=torch.long, device=dev)
+        mask = None
+        if limit is not None:
+            keys = torch.arange(L, device=dev)
+            mask = torch.where(keys[None, :] < limit.view(B, 1), 0.0, float('-inf')).to(torch.bfloat16)
+            mask = mask.view(B, 1, 1, L)
         q = self._gemm(row_q8, row_s8, lay.qkv_w[:qd], lay.qkv_s[:qd])
-        torch.ops.mica.qk_norm_rope(q, lay.q_norm, None, self.cos, self.sin, pos, 0, cfg.heads, 0, cfg.eps)
-        attn = self._attention(q.view(1, cfg.heads, cfg.head_dim), k.view(S, cfg.kv_heads, cfg.head_dim),
-                               v.view(S, cfg.kv_heads, cfg.head_dim), causal=False, mask=mask)
+        torch.ops.mica.qk_norm_rope(q, lay.q_norm, None, self.cos, self.sin, qpos, 0, cfg.heads, 0, cfg.eps)
+        attn = self._attention(q.view(B, 1, cfg.heads, cfg.head_dim), k.view(B, L, cfg.kv_heads, cfg.head_dim),
+                               v.view(B, L, cfg.kv_heads, cfg.head_dim), causal=False, mask=mask)
         qa, sa = torch.ops.mica.act_quant(attn, None, K._round_code())
         o = self._gemm(qa, sa, lay.o_w, lay.o_s)
         q8r, s8r, res = self._norm_quant(o, lay.post_norm, res)
@@ -308,6 +315,26 @@ class Prefill:
         if hi_t is not None and lo_t is None:
             lo_t = torch.zeros(1, dtype=torch.int32, device=dev)
         return self.probs(self.hidden_last(ids, limit), lo_t, hi_t)
+
+    @torch.no_grad()
+    def score_batch(self, ids_list, slices=None):
+        """Scores several requests in one pass: ids padded to [B, L] (L a multiple of 64),
+        each request's own length as its limit, per-request option slices (lo, hi).
+        Returns (logits, probs) fp32 [B, n_rows]. Used for batches of similar lengths, like
+        the reference's shaped batching (v0.5/serving/lib/release_runtime.py:1156-1227)."""
+        dev = self.m.device
+        B = len(ids_list)
+        lens = [int(t.shape[0]) for t in ids_list]
+        L = self.bucket(max(lens))
+        ids = torch.zeros(B, L, dtype=torch.long, device=dev)
+        for i, t in enumerate(ids_list):
+            ids[i, :lens[i]].copy_(t)
+        limit = torch.tensor(lens, dtype=torch.long, device=dev)
+        lo = hi = None
+        if slices is not None:
+            lo = torch.tensor([int(a) for a, _ in slices], dtype=torch.int32, device=dev)
+            hi = torch.tensor([int(b) for _, b in slices], dtype=torch.int32, device=dev)
+        return self.probs(self.hidden_last(ids, limit), lo, hi)
 
     # ---- CUDA graphs ------------------------------------------------------------------------
     def bucket(self, n: int) -> int:

@@ -109,3 +109,27 @@ def tune(shapes, device='cuda', reps: int = 20, state_dir=None) -> dict:
         set_state_dir(p)
     del ops
     return out
+
+
+MODEL_SHAPES = ((6144, 2560), (2560, 4096), (19456, 2560), (2560, 9728), (2048, 2560), (4096, 2560))
+CLASS_M = (64, 256, 1024, 8192)     # one M per class s / m / n / l
+
+
+def main(argv=None):
+    """python -m mica_b200.tiles --tune --state-dir DIR  (the `--kernel-tune full` step):
+    sweeps the tile choices on this GPU for the 4B model's projections and M-classes and
+    writes DIR/tiles_sm100a.json."""
+    import argparse
+    ap = argparse.ArgumentParser()
+    ap.add_argument('--tune', action='store_true')
+    ap.add_argument('--state-dir', required=True)
+    ap.add_argument('--reps', type=int, default=10)
+    a = ap.parse_args(argv)
+    if a.tune:
+        shapes = [(n, k, m) for n, k in MODEL_SHAPES for m in CLASS_M]
+        res = tune(shapes, reps=a.reps, state_dir=a.state_dir)
+        print(json.dumps(res, indent=1, sort_keys=True))
+
+
+if __name__ == '__main__':
+    main()

@@ -144,3 +144,21 @@ def test_startup_selftest_like_the_reference():
     assert res['ok'], res
     assert res['checked'] == 3 * 2 * len(rt.SELFTEST_ROWS)
     assert res['worst_ratio'] <= rt.SELFTEST_TOL
+
+
+def test_batched_scoring_matches_single_requests():
+    """[B, L] batches (padded, per-request limits and option slices) give each request the
+    probabilities it gets alone (within attention-kernel rounding)."""
+    from mica_b200 import prefill as P
+    cfg = P.DecoderConfig(layers=3, vocab=4096)
+    model = P.random_decoder(cfg, torch.device('cuda'), seed=21)
+    pf = P.Prefill(model, torch.arange(0, 257), max_len=4096)
+    gen = torch.Generator().manual_seed(8)
+    lens = [300, 511, 64, 1000, 777]
+    ids = [torch.randint(0, cfg.vocab, (n,), generator=gen).cuda() for n in lens]
+    slices = [(2, 2 + 10 * (i + 1)) for i in range(len(lens))]
+    zb, pb = pf.score_batch(ids, slices)
+    for i, t in enumerate(ids):
+        z1, p1 = pf.score(t, *slices[i], graphs=False)
+        assert torch.allclose(pb[i:i + 1], p1, atol=2e-3, rtol=0), i
+        assert abs(float(pb[i].sum()) - 1.0) < 1e-4
