@@ -618,10 +618,15 @@ int mica_qk_norm_rope(void* qkv, long ld, const void* q_w, const void* k_w, cons
     a.q_w = static_cast<const __nv_bfloat16*>(q_w); a.k_w = static_cast<const __nv_bfloat16*>(k_w);
     a.cos = static_cast<const __nv_bfloat16*>(cos); a.sin = static_cast<const __nv_bfloat16*>(sin);
     a.pos = reinterpret_cast<const long*>(pos); a.pos0 = pos0; a.S = S; a.H = H; a.KV = KV; a.eps = eps;
-    const unsigned blocks = static_cast<unsigned>((warps * 32 + 255) / 256);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    if (D == 128) qk_norm_rope_kernel<128><<<blocks, 256, 0, st>>>(a);
-    else qk_norm_rope_kernel<64><<<blocks, 256, 0, st>>>(a);
+    if (D == 128) {
+        // one warp per token (cos/sin and weights held across the token's heads)
+        const unsigned blocks = static_cast<unsigned>((static_cast<long>(S) * 32 + 255) / 256);
+        qk_norm_rope_token_kernel<<<blocks, 256, 0, st>>>(a);
+    } else {
+        const unsigned blocks = static_cast<unsigned>((warps * 32 + 255) / 256);
+        qk_norm_rope_kernel<64><<<blocks, 256, 0, st>>>(a);
+    }
     return launch_status();
 }
 

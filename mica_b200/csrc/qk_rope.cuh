@@ -94,4 +94,55 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(const QkRopeArgs a) {
     }
 }
 
+// One warp per token for D = 128: lane l owns dims (2l, 2l+1) and their rotation partners
+// (64+2l, 64+2l+1). cos/sin of the token and both norm weights stay in registers across the
+// token's H + KV heads; each head costs two 4-byte loads and stores per lane. Every step is
+// fp32 arithmetic followed by an explicit bf16 rounding, the HF op sequence.
+__global__ void __launch_bounds__(256) qk_norm_rope_token_kernel(const QkRopeArgs a) {
+    constexpr int D = 128;
+    const long s = (static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (s >= a.S) return;
+    const long p = a.pos ? a.pos[s] : a.pos0 + s;
+    const int d = 2 * lane;
+    const __nv_bfloat162 c_lo = *reinterpret_cast<const __nv_bfloat162*>(a.cos + p * D + d);
+    const __nv_bfloat162 c_hi = *reinterpret_cast<const __nv_bfloat162*>(a.cos + p * D + D / 2 + d);
+    const __nv_bfloat162 s_lo = *reinterpret_cast<const __nv_bfloat162*>(a.sin + p * D + d);
+    const __nv_bfloat162 s_hi = *reinterpret_cast<const __nv_bfloat162*>(a.sin + p * D + D / 2 + d);
+    __nv_bfloat162 wq_lo = __float2bfloat162_rn(0.f), wq_hi = wq_lo, wk_lo = wq_lo, wk_hi = wq_lo;
+    if (a.H > 0) {
+        wq_lo = *reinterpret_cast<const __nv_bfloat162*>(a.q_w + d);
+        wq_hi = *reinterpret_cast<const __nv_bfloat162*>(a.q_w + D / 2 + d);
+    }
+    if (a.KV > 0) {
+        wk_lo = *reinterpret_cast<const __nv_bfloat162*>(a.k_w + d);
+        wk_hi = *reinterpret_cast<const __nv_bfloat162*>(a.k_w + D / 2 + d);
+    }
+    __nv_bfloat16* row = a.qkv + s * a.ld;
+    const int heads = a.H + a.KV;
+#pragma unroll 2
+    for (int h = 0; h < heads; ++h) {
+        __nv_bfloat16* x = row + static_cast<long>(h) * D;
+        const __nv_bfloat162 xl = *reinterpret_cast<const __nv_bfloat162*>(x + d);
+        const __nv_bfloat162 xh = *reinterpret_cast<const __nv_bfloat162*>(x + D / 2 + d);
+        const float2 fl = __bfloat1622float2(xl), fh = __bfloat1622float2(xh);
+        float ss = __fadd_rn(__fadd_rn(__fmul_rn(fl.x, fl.x), __fmul_rn(fl.y, fl.y)),
+                             __fadd_rn(__fmul_rn(fh.x, fh.x), __fmul_rn(fh.y, fh.y)));
+        ss = warp_sum(ss);
+        const float r = __frsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(D)), a.eps));
+        const bool is_q = h < a.H;
+        const float2 wl = __bfloat1622float2(is_q ? wq_lo : wk_lo), wh = __bfloat1622float2(is_q ? wq_hi : wk_hi);
+        const float2 cl = __bfloat1622float2(c_lo), ch = __bfloat1622float2(c_hi);
+        const float2 sl = __bfloat1622float2(s_lo), sh = __bfloat1622float2(s_hi);
+        const float yl0 = bf(__fmul_rn(wl.x, bf(__fmul_rn(fl.x, r)))), yl1 = bf(__fmul_rn(wl.y, bf(__fmul_rn(fl.y, r))));
+        const float yh0 = bf(__fmul_rn(wh.x, bf(__fmul_rn(fh.x, r)))), yh1 = bf(__fmul_rn(wh.y, bf(__fmul_rn(fh.y, r))));
+        const float ol0 = __fadd_rn(bf(__fmul_rn(yl0, cl.x)), bf(__fmul_rn(-yh0, sl.x)));
+        const float ol1 = __fadd_rn(bf(__fmul_rn(yl1, cl.y)), bf(__fmul_rn(-yh1, sl.y)));
+        const float oh0 = __fadd_rn(bf(__fmul_rn(yh0, ch.x)), bf(__fmul_rn(yl0, sh.x)));
+        const float oh1 = __fadd_rn(bf(__fmul_rn(yh1, ch.y)), bf(__fmul_rn(yl1, sh.y)));
+        *reinterpret_cast<__nv_bfloat162*>(x + d) = __floats2bfloat162_rn(ol0, ol1);
+        *reinterpret_cast<__nv_bfloat162*>(x + D / 2 + d) = __floats2bfloat162_rn(oh0, oh1);
+    }
+}
+
 }  // namespace mica

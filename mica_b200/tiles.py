@@ -87,18 +87,29 @@ def tune(shapes, device='cuda', reps: int = 20, state_dir=None) -> dict:
         sx = torch.rand(m, generator=g, device=dev) * 1e-2 + 1e-3
         sw = torch.rand(n, generator=g, device=dev) * 1e-2 + 1e-3
         best, best_t = 0, float('inf')
-        for bn in CHOICES:
-            for _ in range(3):
-                torch.ops.mica.w8a8_gemm(qx, sx, qw, sw, None, 0, bn)
+        for tile_code in CHOICES:
+            # time `reps` back-to-back launches replayed from a CUDA graph: device time only,
+            # no per-launch Python overhead (which would swamp small shapes)
+            s = torch.cuda.Stream(device=dev)
+            s.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(s):
+                for _ in range(3):
+                    torch.ops.mica.w8a8_gemm(qx, sx, qw, sw, None, 0, tile_code)
+            torch.cuda.current_stream(dev).wait_stream(s)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                for _ in range(reps):
+                    torch.ops.mica.w8a8_gemm(qx, sx, qw, sw, None, 0, tile_code)
+            graph.replay()
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record()
-            for _ in range(reps):
-                torch.ops.mica.w8a8_gemm(qx, sx, qw, sw, None, 0, bn)
+            graph.replay()
             b.record()
             b.synchronize()
             t = a.elapsed_time(b) / reps
+            del graph
             if t < best_t:
-                best, best_t = bn, t
+                best, best_t = tile_code, t
         out[key(n, k, m)] = best
     if state_dir:
         p = Path(state_dir)
