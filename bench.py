@@ -341,11 +341,12 @@ def run_mica(args, rank, world, local):
     pk = peaks()
     peak_int8 = 2 * pk['bf16']
     achieved = gemm_ops / (gemm_ms * 1e-3) / 1e12
-    traffic = None
+    traffic, alg_bytes = None, None
     prof = ROOT / 'profiles' / 'gemm_i8_traffic.json'
     if prof.is_file():
         try:
-            traffic = json.loads(prof.read_text()).get('traffic_bytes_per_launch_avg')
+            tj = json.loads(prof.read_text())
+            traffic, alg_bytes = tj.get('traffic_bytes_per_launch_avg'), tj.get('algorithmic_bytes_per_launch_avg')
         except ValueError:
             traffic = None
     line = {
@@ -357,6 +358,9 @@ def run_mica(args, rank, world, local):
         'gpu_launches': launches_per_step * args.steps,
         'roofline': {'bound': 'tensor', 'achieved': round(achieved, 1), 'peak': round(peak_int8, 1),
                      'unit': 'TOPS (int8)', 'frac': round(achieved / peak_int8, 4), 'traffic': traffic,
+                     'traffic_note': ('DRAM bytes per GEMM launch, mean over the sweep, one ncu capture '
+                                      '(profiles/gemm_i8_traffic.json); algorithmic bytes per launch '
+                                      f'(A + B + bf16 C + scales) {alg_bytes}'),
                      'peak_source': f"2 x {pk['source']} bf16 dense ({pk['bf16']} TFLOP/s); nominal dense int8 4500",
                      'frac_of_nominal_4500': round(achieved / 4500.0, 4)},
         'clocks': clocks,
@@ -580,9 +584,12 @@ def run_shape(args):
     import mica_b200.int8_kernels as K
     from mica_b200 import _native as Nat
     from mica_b200.int8_runtime import interleave_gate_up
-    m, n, k = (int(v) for v in args.shape.split(','))
     dev = torch.device('cuda', 0)
     K.preload(dev)
+    if args.shape == 'sweep':
+        run_sweep_launches(args, dev)
+        return
+    m, n, k = (int(v) for v in args.shape.split(','))
     g = torch.Generator(device=dev).manual_seed(7)
     x = torch.randn(m, k, generator=g, device=dev).to(torch.bfloat16)
     w = torch.randint(-127, 128, (n, k), generator=g, device=dev, dtype=torch.int8)
@@ -630,6 +637,27 @@ def run_shape(args):
                       unit: round(rate, 1)}), flush=True)
 
 
+def run_sweep_launches(args, dev):
+    """The config-1 sweep's 16 GEMMs, each launched once per step after an L2 flush, in sweep
+    order: the launch list that a one-pass DRAM-traffic capture reads (`--shape sweep`)."""
+    import torch
+    g = torch.Generator(device=dev).manual_seed(1234)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    for _ in range(args.warmup + args.steps):
+        for m in MS:
+            for name, n, k in PROJECTIONS:
+                w = torch.randint(-127, 128, (n, k), generator=g, device=dev, dtype=torch.int8)
+                sw = torch.rand(n, generator=g, device=dev) * 9e-3 + 1e-3
+                x = torch.randn(m, k, generator=g, device=dev).to(torch.bfloat16)
+                q, s = torch.ops.mica.act_quant(x, None, 0)
+                flush.fill_(1)
+                y = torch.ops.mica.w8a8_gemm(q, s, w, sw, None, 0, args.tile)
+                torch.cuda.synchronize(dev)
+                del w, sw, x, q, s, y
+    print(json.dumps({'sweep_launches': args.warmup + args.steps, 'gemms_per_step': len(MS) * len(PROJECTIONS)}),
+          flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument('--gpus', type=int, default=1)
@@ -637,7 +665,8 @@ def main():
     ap.add_argument('--warmup', type=int, default=5)
     ap.add_argument('--impl', choices=('mica', 'reference'), default='mica')
     ap.add_argument('--cpu-seconds', type=float, default=10.0)
-    ap.add_argument('--shape', default=None, help='M,N,K: time one kernel on one shape (profiling)')
+    ap.add_argument('--shape', default=None,
+                    help='M,N,K: time one kernel on one shape; sweep: the config-1 GEMMs once each (profiling)')
     ap.add_argument('--kernel', default='gemm', help='gemm | swiglu | act_quant | rmsnorm_quant | qk_rope | readout')
     ap.add_argument('--tile', type=int, default=0, help='block_m*1000+block_n, 0 = library choice')
     ap.add_argument('--skip-model', action='store_true', help='only the config-1 GEMM sweep')

@@ -126,6 +126,13 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void*
                  ::"l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(src)), "r"(x), "r"(y)
                  : "memory");
 }
+// Same with an L2 cache-policy hint (createpolicy value).
+__device__ __forceinline__ void tma_store_2d_hint(const CUtensorMap* map, const void* src, int x, int y,
+                                                  uint64_t policy) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group.L2::cache_hint [%0, {%2, %3}], [%1], %4;"
+                 ::"l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(src)), "r"(x), "r"(y), "l"(policy)
+                 : "memory");
+}
 __device__ __forceinline__ void tma_store_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 template <int N>
 __device__ __forceinline__ void tma_store_wait_read() {
@@ -233,14 +240,15 @@ __device__ __forceinline__ void cluster_sync() {
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
-// TMA load into this CTA's shared memory whose completion bytes are counted on the
-// mbarrier at `bar_cluster_addr` (the even CTA's barrier for the pair).
-__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t bar_cluster_addr, int x,
-                                                 int y, uint64_t policy) {
+// TMA load into the shared memory of either CTA of the pair (`dst_cluster_addr`, a
+// shared::cluster address) whose completion bytes are counted on the mbarrier at
+// `bar_cluster_addr`, which may also live in either CTA (the .cta_group::2 form).
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst_cluster_addr, const CUtensorMap* map,
+                                                 uint32_t bar_cluster_addr, int x, int y, uint64_t policy) {
     asm volatile(
         "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
         " [%0], [%1, {%2, %3}], [%4], %5;"
-        ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar_cluster_addr),
+        ::"r"(dst_cluster_addr), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar_cluster_addr),
         "l"(policy)
         : "memory");
 }

@@ -214,6 +214,8 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
         uint8_t* my_boxes = smem_epi + ew * S::BOX_BUFS * S::BOX_BYTES;
         int box_count = 0;
         int local = 0;
+        // The dequantised output is written once: evict it before the weights (evict_last).
+        const uint64_t pol_c = policy_evict_first();
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
             const int m0 = (tile / num_n) * S::BM;
             const int n0 = (tile % num_n) * BN;
@@ -292,7 +294,7 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
                     __syncwarp();
                     if (lane == 0) {
                         const int x = n0 + bx * COLS_PER_BOX, y = m0 + q4 * 32;
-                        if (x < N && y < M) tma_store_2d(&tmap_c, box, x, y);   // boxes past the edge hold nothing
+                        if (x < N && y < M) tma_store_2d_hint(&tmap_c, box, x, y, pol_c);   // edge boxes hold nothing
                         tma_store_commit();
                     }
                 }

@@ -2,14 +2,20 @@
 //
 // A cluster of two CTAs on two SMs computes one 256 x BN tile with a single stream of
 // tcgen05.mma.cta_group::2.kind::i8 instructions (256 x BN x 32 each) issued by the even
-// CTA. Each CTA loads 128 rows of A and BN/2 rows of B per stage into its own shared memory
+// CTA. Each CTA holds 128 rows of A and BN/2 rows of B per stage in its own shared memory
 // (at identical offsets), so per SM the MMA reads 16 KB of A and 16 KB of B per 128-byte K
 // step instead of 16 + 32 KB in the single-CTA kernel: a third less shared-memory and L2
 // traffic for the same work, and room for six stages instead of four.
 //
+// The even CTA's producer issues all four loads of a stage: the .cta_group::2 TMA form
+// writes the odd CTA's half into its shared memory and still completes on the even CTA's
+// barrier. Every stage completion is then local to the MMA issuer. When each CTA loaded its
+// own half, the odd CTA's two completions per stage crossed the pair and, on B200, cost the
+// main loop about a seventh of its rate. The odd CTA runs no producer.
+//
 // Synchronisation (all waits bounded, as in gemm_i8.cuh):
-//   full[s]    even CTA only: both CTAs' TMA loads complete their bytes on it;
-//   empty[s]   per CTA: the even CTA's MMA commit arrives on both CTAs' copies;
+//   full[s]    even CTA: its four TMA loads of the stage complete their bytes on it;
+//   empty[s]   even CTA: the MMA commit of the stage arrives on it;
 //   tfull[a]   per CTA: the even CTA's last commit of a tile arrives on both copies;
 //   tempty[a]  even CTA only: all 256 epilogue threads of the pair arrive on it.
 // Epilogue and semantics are those of gemm_i8_kernel (dequant, no FMA, TMA store).
@@ -100,8 +106,8 @@ gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
     const uint32_t tmem_base = *tmem_slot;
 
     if (warp == 0) {
-        // ------------------------------- TMA producer (both CTAs) --------------------
-        if (lane == 0) {
+        // ------------------------------- TMA producer (even CTA) ---------------------
+        if (leader && lane == 0) {
             uint32_t it = 0;
             bool ok = true;
             const uint64_t pol_b = policy_evict_last();
@@ -116,20 +122,23 @@ gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
                         ok = false;
                         break;
                     }
-                    const uint32_t full0 = map_to_rank(smem_u32(&full_bar[st]), 0);
-                    if (leader) mbar_arrive_expect_tx(&full_bar[st], 2 * S::STAGE_BYTES);
-                    tma_load_2d_pair(smem_a + st * S::A_BYTES, &tmap_a, full0, kb * S::BK,
-                                     m0 + static_cast<int>(rank) * 128, pol_a);
-                    tma_load_2d_pair(smem_b + st * S::B_BYTES, &tmap_b, full0, kb * S::BK,
-                                     n0 + static_cast<int>(rank) * (BN / 2), pol_b);
+                    const uint32_t full = smem_u32(&full_bar[st]);
+                    const uint32_t a_st = smem_u32(smem_a + st * S::A_BYTES);
+                    const uint32_t b_st = smem_u32(smem_b + st * S::B_BYTES);
+                    mbar_arrive_expect_tx(&full_bar[st], 2 * S::STAGE_BYTES);
+                    for (uint32_t r = 0; r < 2; ++r) {
+                        tma_load_2d_pair(map_to_rank(a_st, r), &tmap_a, full, kb * S::BK,
+                                         m0 + static_cast<int>(r) * 128, pol_a);
+                        tma_load_2d_pair(map_to_rank(b_st, r), &tmap_b, full, kb * S::BK,
+                                         n0 + static_cast<int>(r) * (BN / 2), pol_b);
+                    }
                 }
             }
-            if (leader) {
-                // Drain: the pair's last loads of each stage land before shared memory goes away.
-                const uint32_t first = it > static_cast<uint32_t>(STAGES) ? it - STAGES : 0u;
-                for (uint32_t j = first; j < it; ++j)
-                    mbar_wait(&full_bar[j % STAGES], (j / STAGES) & 1u, abort_flag, MICA_DEV_TIMEOUT_DRAIN);
-            }
+            // Drain: the pair's last loads of each stage land before shared memory goes away
+            // (the odd CTA waits for this warp at the closing cluster barrier).
+            const uint32_t first = it > static_cast<uint32_t>(STAGES) ? it - STAGES : 0u;
+            for (uint32_t j = first; j < it; ++j)
+                mbar_wait(&full_bar[j % STAGES], (j / STAGES) & 1u, abort_flag, MICA_DEV_TIMEOUT_DRAIN);
         }
         __syncwarp();
     } else if (warp == 1) {
@@ -163,9 +172,7 @@ gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
                             mma_i8_pair(d_tmem, smem_desc_k128(a_addr + k * S::UMMA_K),
                                         smem_desc_k128(b_addr + k * S::UMMA_K), idesc, (kb | k) != 0 ? 1u : 0u);
                         }
-                        const uint32_t e = smem_u32(&empty_bar[st]);
-                        mma_commit_pair(map_to_rank(e, 0));
-                        mma_commit_pair(map_to_rank(e, 1));
+                        mma_commit_pair(map_to_rank(smem_u32(&empty_bar[st]), 0));
                         if (kb == num_kb - 1) {
                             const uint32_t f = smem_u32(&tfull_bar[acc]);
                             mma_commit_pair(map_to_rank(f, 0));
@@ -189,6 +196,7 @@ gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
         uint8_t* my_boxes = smem_epi + ew * 2 * S::BOX_BYTES;
         int box_count = 0;
         int local = 0;
+        const uint64_t pol_c = policy_evict_first();   // output: written once, leave L2 to the weights
         constexpr int COLS_PER_BOX = 128 / static_cast<int>(sizeof(OutT));
         constexpr int CHUNKS_PER_BOX = COLS_PER_BOX / 32;
         constexpr int BOXES = BN / COLS_PER_BOX;
@@ -259,7 +267,7 @@ gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
                 __syncwarp();
                 if (lane == 0) {
                     const int x = n0 + bx * COLS_PER_BOX, y = m0 + static_cast<int>(rank) * 128 + q4 * 32;
-                    if (x < N && y < M) tma_store_2d(&tmap_c, box, x, y);   // boxes past the edge hold nothing
+                    if (x < N && y < M) tma_store_2d_hint(&tmap_c, box, x, y, pol_c);   // edge boxes hold nothing
                     tma_store_commit();
                 }
             }
