@@ -307,6 +307,33 @@ __device__ __forceinline__ int quant_round(float v, int round_mode) {
     return min(max(r, -127), 127);
 }
 
+// The same rounding without the +-127 clamp, for quantisers whose scale comes from the
+// absmax of the very values they quantise. With s = RN(max(amax, 1e-8) / 127) and
+// |x| <= amax, x / s <= 127 / (1 - 2^-24), so |RN(x / s)| <= 127 + 2^-17 (the fp32 spacing
+// at 127) and both modes give |q| <= 127: the reference's clamp never acts on finite input.
+template <int MODE>
+__device__ __forceinline__ int quant_code(float v) {
+    if constexpr (MODE == MICA_ROUND_HALF_EVEN) return __float2int_rn(v);
+    else return __float2int_rz(__fadd_rn(v, copysignf(0.5f, v)));
+}
+// Four codes, each within int8 range, packed little-endian (q0 in the low byte) by two
+// saturating pack instructions: cvt.pack.sat d, a, b, c puts sat(b) in bits 0-7, sat(a) in
+// bits 8-15 and the low half of c in bits 16-31.
+__device__ __forceinline__ uint32_t pack4_s8(int q0, int q1, int q2, int q3) {
+    uint32_t hi, w;
+    asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, %3;" : "=r"(hi) : "r"(q3), "r"(q2), "r"(0));
+    asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, %3;" : "=r"(w) : "r"(q1), "r"(q0), "r"(hi));
+    return w;
+}
+// Eight values quantised with RN(x / s) (div_by_scale) into two packed words.
+template <int MODE>
+__device__ __forceinline__ uint2 quant8(const float (&v)[8], float scale, float rscale) {
+    int q[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) q[e] = quant_code<MODE>(div_by_scale(v[e], scale, rscale));
+    return make_uint2(pack4_s8(q[0], q[1], q[2], q[3]), pack4_s8(q[4], q[5], q[6], q[7]));
+}
+
 }  // namespace mica
 
 // ---- host helpers --------------------------------------------------------------------

@@ -81,6 +81,40 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t
                  : "memory");
 }
 
+// Phase 2 of the fused SwiGLU kernel: each warp requantises whole rows of h [M, N/2] with
+// the row scale from the absmax that phase 1 accumulated (row_amax).
+template <int MODE>
+__device__ __forceinline__ void swiglu_requant_rows(const GemmArgs& args, int warp, int lane) {
+    const int I = args.N / 2;
+    const int warps_total = gridDim.x * (blockDim.x >> 5);
+    for (int row = blockIdx.x * (blockDim.x >> 5) + warp; row < args.M; row += warps_total) {
+        const unsigned bits = __ldcg(args.row_amax + row);
+        const float scale = __fdiv_rn(fmaxf(__uint_as_float(bits), 1e-8f), 127.0f);
+        const float rscale = __frcp_rn(scale);
+        const __nv_bfloat16* hrow = args.h + static_cast<long>(row) * args.ldh;
+        int8_t* qrow = args.q_out + static_cast<long>(row) * args.ldq;
+        // two 8-element vectors per lane per step: 16 independent divisions in flight
+        for (int c = lane * 8; c < I; c += 32 * 8 * 2) {
+            const int c2 = c + 32 * 8;
+            const bool has2 = c2 < I;
+            const uint4 v0 = __ldcg(reinterpret_cast<const uint4*>(hrow + c));
+            const uint4 v1 = has2 ? __ldcg(reinterpret_cast<const uint4*>(hrow + c2)) : make_uint4(0, 0, 0, 0);
+            float f0[8], f1[8];
+            const uint32_t w0[4] = {v0.x, v0.y, v0.z, v0.w}, w1[4] = {v1.x, v1.y, v1.z, v1.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                f0[2 * j] = __uint_as_float(w0[j] << 16);
+                f0[2 * j + 1] = __uint_as_float(w0[j] & 0xFFFF0000u);
+                f1[2 * j] = __uint_as_float(w1[j] << 16);
+                f1[2 * j + 1] = __uint_as_float(w1[j] & 0xFFFF0000u);
+            }
+            *reinterpret_cast<uint2*>(qrow + c) = quant8<MODE>(f0, scale, rscale);
+            if (has2) *reinterpret_cast<uint2*>(qrow + c2) = quant8<MODE>(f1, scale, rscale);
+        }
+        if (lane == 0) args.s_out[row] = scale;
+    }
+}
+
 template <int BN, int EPI, typename OutT, int EW = 4>
 __global__ void __launch_bounds__(64 + 32 * EW, 1)
 gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
@@ -408,34 +442,8 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
         }
         __syncthreads();
         if (*abort_flag) return;
-        const int I = N / 2;
-        const int warps_total = gridDim.x * (blockDim.x >> 5);
-        for (int row = blockIdx.x * (blockDim.x >> 5) + warp; row < M; row += warps_total) {
-            const unsigned bits = __ldcg(args.row_amax + row);
-            const float scale = __fdiv_rn(fmaxf(__uint_as_float(bits), 1e-8f), 127.0f);
-            const float rscale = __frcp_rn(scale);
-            const __nv_bfloat16* hrow = args.h + static_cast<long>(row) * args.ldh;
-            int8_t* qrow = args.q_out + static_cast<long>(row) * args.ldq;
-            // two 8-element vectors per lane per step: 16 independent divisions in flight
-            for (int c = lane * 8; c < I; c += 32 * 8 * 2) {
-                const int c2 = c + 32 * 8;
-                const bool has2 = c2 < I;
-                const uint4 v0 = __ldcg(reinterpret_cast<const uint4*>(hrow + c));
-                const uint4 v1 = has2 ? __ldcg(reinterpret_cast<const uint4*>(hrow + c2)) : make_uint4(0, 0, 0, 0);
-                const uint32_t w8[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-                uint32_t out[4] = {0u, 0u, 0u, 0u};
-#pragma unroll
-                for (int e = 0; e < 16; ++e) {
-                    const uint32_t half = (w8[e >> 1] >> ((e & 1) * 16)) & 0xFFFFu;
-                    const float x = __uint_as_float(half << 16);
-                    const int qv = quant_round(div_by_scale(x, scale, rscale), args.round_mode);
-                    out[e >> 2] |= (static_cast<uint32_t>(qv) & 0xFFu) << ((e & 3) * 8);
-                }
-                *reinterpret_cast<uint2*>(qrow + c) = make_uint2(out[0], out[1]);
-                if (has2) *reinterpret_cast<uint2*>(qrow + c2) = make_uint2(out[2], out[3]);
-            }
-            if (lane == 0) args.s_out[row] = scale;
-        }
+        if (args.round_mode == MICA_ROUND_HALF_EVEN) swiglu_requant_rows<MICA_ROUND_HALF_EVEN>(args, warp, lane);
+        else swiglu_requant_rows<MICA_ROUND_HALF_AWAY>(args, warp, lane);
     }
 }
 

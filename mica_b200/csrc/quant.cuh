@@ -100,11 +100,94 @@ struct QuantArgs {
     int M, K, round_mode;
 };
 
+template <int MODE>
+__device__ __forceinline__ void store_codes(const float (&v)[QV][8], int nvec, float scale, float rscale, int8_t* qr) {
+#pragma unroll
+    for (int i = 0; i < QV; ++i) {
+        const int idx = threadIdx.x + i * blockDim.x;
+        if (idx < nvec) *reinterpret_cast<uint2*>(qr + idx * 8) = quant8<MODE>(v[i], scale, rscale);
+    }
+}
+
+// Element-wise |.| max of eight packed 16-bit floats into `m` (exact: the max of bf16/fp16
+// values is one of them, so converting the final max to fp32 equals the fp32 max).
+template <typename T>
+__device__ __forceinline__ void absmax8(const uint4& w, uint32_t& m) {
+    using T2 = typename std::conditional<std::is_same<T, __half>::value, __half2, __nv_bfloat162>::type;
+    T2 acc = *reinterpret_cast<const T2*>(&m);
+    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc = __hmax2(acc, __habs2(*reinterpret_cast<const T2*>(&ws[j])));
+    m = *reinterpret_cast<const uint32_t*>(&acc);
+}
+
+template <typename T>
+__device__ __forceinline__ void unpack8(const uint4& w, float (&f)[8]) {
+    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        if constexpr (std::is_same<T, __half>::value) {
+            const __half2 h = *reinterpret_cast<const __half2*>(&ws[i]);
+            f[2 * i] = __low2float(h);
+            f[2 * i + 1] = __high2float(h);
+        } else {
+            f[2 * i] = __uint_as_float(ws[i] << 16);
+            f[2 * i + 1] = __uint_as_float(ws[i] & 0xFFFF0000u);
+        }
+    }
+}
+
+// mica_act_quant on 16-bit input without a smoothing vector: the row stays packed in
+// registers (half the registers of the fp32 copy) and the absmax runs on packed pairs.
+template <typename T, int MODE>
+__device__ __forceinline__ void quant_row_packed(const QuantArgs& a, float* red) {
+    const int row = blockIdx.x;
+    const int nvec = a.K >> 3;
+    const T* xr = static_cast<const T*>(a.x) + static_cast<long>(row) * a.ldx;
+    uint4 w[QV];
+    uint32_t m = 0u;
+#pragma unroll
+    for (int i = 0; i < QV; ++i) {
+        const int idx = threadIdx.x + i * blockDim.x;
+        w[i] = idx < nvec ? __ldg(reinterpret_cast<const uint4*>(xr + idx * 8)) : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int i = 0; i < QV; ++i) absmax8<T>(w[i], m);
+    float am;
+    if constexpr (std::is_same<T, __half>::value) {
+        const __half2 h = *reinterpret_cast<const __half2*>(&m);
+        am = fmaxf(__low2float(h), __high2float(h));
+    } else {
+        am = fmaxf(__uint_as_float(m << 16), __uint_as_float(m & 0xFFFF0000u));
+    }
+    am = block_reduce<true>(am, red);
+    const float scale = __fdiv_rn(fmaxf(am, 1e-8f), 127.0f);
+    const float rscale = __frcp_rn(scale);
+    int8_t* qr = a.q + static_cast<long>(row) * a.ldq;
+#pragma unroll
+    for (int i = 0; i < QV; ++i) {
+        const int idx = threadIdx.x + i * blockDim.x;
+        if (idx < nvec) {
+            float f[8];
+            unpack8<T>(w[i], f);
+            *reinterpret_cast<uint2*>(qr + idx * 8) = quant8<MODE>(f, scale, rscale);
+        }
+    }
+    if (threadIdx.x == 0) a.s[row] = scale;
+}
+
 // NORM = false: mica_act_quant. NORM = true: mica_rmsnorm_quant. MAXT bounds the block
 // size (512 for rows up to 16384 elements, 1024 beyond), which bounds registers per thread.
 template <typename T, bool NORM, int MAXT = 512>
 __global__ void __launch_bounds__(MAXT) quant_rows_kernel(const QuantArgs a) {
     __shared__ float red[32];
+    if constexpr (!NORM && sizeof(T) == 2) {
+        if (a.inv == nullptr) {
+            if (a.round_mode == MICA_ROUND_HALF_EVEN) quant_row_packed<T, MICA_ROUND_HALF_EVEN>(a, red);
+            else quant_row_packed<T, MICA_ROUND_HALF_AWAY>(a, red);
+            return;
+        }
+    }
     const int row = blockIdx.x;
     const int nvec = a.K >> 3;
     const T* xr = static_cast<const T*>(a.x) + static_cast<long>(row) * a.ldx;
@@ -185,19 +268,8 @@ __global__ void __launch_bounds__(MAXT) quant_rows_kernel(const QuantArgs a) {
     const float scale = __fdiv_rn(fmaxf(am, 1e-8f), 127.0f);
     const float rscale = __frcp_rn(scale);
     int8_t* qr = a.q + static_cast<long>(row) * a.ldq;
-#pragma unroll
-    for (int i = 0; i < QV; ++i) {
-        const int idx = threadIdx.x + i * blockDim.x;
-        if (idx < nvec) {
-            uint32_t o[2] = {0u, 0u};
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-                const int qv = quant_round(div_by_scale(v[i][e], scale, rscale), a.round_mode);
-                o[e >> 2] |= (static_cast<uint32_t>(qv) & 0xFFu) << ((e & 3) * 8);
-            }
-            *reinterpret_cast<uint2*>(qr + idx * 8) = make_uint2(o[0], o[1]);
-        }
-    }
+    if (a.round_mode == MICA_ROUND_HALF_EVEN) store_codes<MICA_ROUND_HALF_EVEN>(v, nvec, scale, rscale, qr);
+    else store_codes<MICA_ROUND_HALF_AWAY>(v, nvec, scale, rscale, qr);
     if (threadIdx.x == 0) a.s[row] = scale;
 }
 
