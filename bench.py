@@ -396,7 +396,7 @@ def run_chain(dev, reps=20):
 
     def chain():
         q, s, _, _ = torch.ops.mica.rmsnorm_quant(x, None, gamma, None, 1e-6, Nat.NORM_WEIGHT, 0, False, True)
-        _, qh, sh = torch.ops.mica.gemm_swiglu_quant(q, s, wgu, sgu, None, 0)
+        _, qh, sh = torch.ops.mica.gemm_swiglu_quant(q, s, wgu, sgu, None, None, 0)
         return torch.ops.mica.w8a8_gemm(qh, sh, wd, sd, None, 0, 0)
 
     us = _graph_time(dev, chain, reps)
@@ -601,7 +601,7 @@ def run_shape(args):
     elif args.kernel == 'swiglu':
         wgu = interleave_gate_up(w[: n // 2], w[n // 2:])
         sgu = interleave_gate_up(sw[: n // 2], sw[n // 2:])
-        fn, work = (lambda: torch.ops.mica.gemm_swiglu_quant(q, s, wgu, sgu, None, 0)), ('TOPS', 2 * m * n * k)
+        fn, work = (lambda: torch.ops.mica.gemm_swiglu_quant(q, s, wgu, sgu, None, None, 0)), ('TOPS', 2 * m * n * k)
     elif args.kernel == 'act_quant':
         fn, work = (lambda: torch.ops.mica.act_quant(x, None, 0)), ('GB/s', m * k * 3 + 4 * m)
     elif args.kernel == 'rmsnorm_quant':

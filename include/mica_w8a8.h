@@ -85,7 +85,7 @@ typedef struct mica_caps {
     int pair_clusters;      /* co-resident CTA pairs for the 256-row GEMM tiles         */
 } mica_caps;
 
-#define MICA_ABI_VERSION 1
+#define MICA_ABI_VERSION 2
 
 /* Capability query. Replaces int8_kernels.available() (v0.5/serving/lib/int8_kernels.py:146-159)
  * and the capability probe in _device_cc (:130-143). Fills *caps for `device`.         */
@@ -159,7 +159,11 @@ int mica_w8a8_gemm_cfg(const int8_t* A, long lda, const int8_t* B, long ldb,
  *        (rows 32j..32j+15 = gate rows 16j..16j+15, rows 32j+16..32j+31 = up rows
  *         16j..16j+15); sgu, bias_gu follow the same order (bias_gu may be NULL).
  *   g = bf16(deq(gate)), u = bf16(deq(up)),  h = bf16( bf16(silu(g)) * u )  -> h_out [M, I]
- *   then q_out / s_out = per-token int8 quantisation of h (round_mode as above).
+ *   then q_out / s_out = per-token int8 quantisation of h * inv_h (round_mode as above);
+ *   inv_h [I] is down_proj's inv_smooth, or NULL (v0.5/serving/lib/int8_quant.py:64-67).
+ * gate_proj and up_proj must share their input quantisation (no smoothing, or the same
+ * inv_smooth, applied by the caller's act_quant / rmsnorm_quant); with different smoothing
+ * use two mica_w8a8_gemm calls and mica_swiglu_quant.
  * Replaces gate_proj + up_proj QLinears, fused_kernels.swi_glu
  * (v0.5/serving/lib/fused_kernels.py:85-96, kernel :37-44) and the act_quant of
  * down_proj's input (v0.5/serving/lib/fast_runtime.py:126-132).
@@ -168,6 +172,7 @@ int mica_w8a8_gemm_cfg(const int8_t* A, long lda, const int8_t* B, long ldb,
 size_t mica_swiglu_workspace_bytes(int M);
 int mica_w8a8_gemm_swiglu_quant(const int8_t* A, long lda, const int8_t* Bgu, long ldb,
                                 const float* sa, const float* sgu, const float* bias_gu,
+                                const float* inv_h,
                                 void* h_out, long ldh,
                                 int8_t* q_out, long ldq, float* s_out,
                                 int M, int I, int K, int round_mode,
@@ -195,9 +200,23 @@ int mica_w8a8_gemm_swiglu_quant(const int8_t* A, long lda, const int8_t* Bgu, lo
 #define MICA_NOALLOC_SCRATCH_BYTES  (65536 * 4 + 16)
 int mica_w8a8_gemm_swiglu_quant_noalloc(const int8_t* A, long lda, const int8_t* Bgu, long ldb,
                                         const float* sa, const float* sgu, const float* bias_gu,
+                                        const float* inv_h,
                                         void* h_out, long ldh,
                                         int8_t* q_out, long ldq, float* s_out,
                                         int M, int I, int K, int round_mode, void* stream);
+
+/* SwiGLU of two projection outputs, then down_proj's per-token quantisation:
+ *   h = bf16( bf16(silu(g)) * u )  -> h_out [M, I] (optional),
+ *   q / s = per-token int8 quantisation of h * inv (inv [I] optional; q and s together,
+ *           optional; at least one of h_out and q).
+ * For MLPs whose gate_proj and up_proj have different smoothing (two quantisations of the
+ * same input, so no shared GEMM operand). Replaces fused_kernels.swi_glu
+ * (v0.5/serving/lib/fused_kernels.py:85-96, kernel :37-44) and the act_quant that
+ * down_proj's QLinear runs on its output (v0.5/serving/lib/int8_runtime.py:181-182).
+ * g, u: dtype MICA_DT_BF16 / MICA_DT_FP16 [M, I] with row strides ldg, ldu; I % 8 == 0.   */
+int mica_swiglu_quant(const void* g, long ldg, const void* u, long ldu, int dtype, const float* inv,
+                      void* h_out, long ldh, int8_t* q, long ldq, float* s,
+                      int M, int I, int round_mode, void* stream);
 
 /* Option-logit scorer for the last position of each request:
  *   hn[b]       = optional RMSNorm of h[b] (gamma NULL = h used as given; gamma has

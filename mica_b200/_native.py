@@ -73,12 +73,13 @@ SIGNATURES = {
     'mica_swiglu_workspace_bytes': (_Z, [_I]),
     'mica_w8a8_gemm_swiglu_quant': (
         _I,
-        [_P, _L, _P, _L, _P, _P, _P, _P, _L, _P, _L, _P, _I, _I, _I, _I, _P, _Z, _P],
+        [_P, _L, _P, _L, _P, _P, _P, _P, _P, _L, _P, _L, _P, _I, _I, _I, _I, _P, _Z, _P],
     ),
     'mica_w8a8_gemm_swiglu_quant_noalloc': (
         _I,
-        [_P, _L, _P, _L, _P, _P, _P, _P, _L, _P, _L, _P, _I, _I, _I, _I, _P],
+        [_P, _L, _P, _L, _P, _P, _P, _P, _P, _L, _P, _L, _P, _I, _I, _I, _I, _P],
     ),
+    'mica_swiglu_quant': (_I, [_P, _L, _P, _L, _I, _P, _P, _L, _P, _L, _P, _I, _I, _I, _P]),
     'mica_option_logits': (_I, [_P, _I, _L, _P, _I, _F, _P, _I, _I, _P, _P, _P, _P, _I, _P]),
     'mica_qk_norm_rope': (_I, [_P, _L, _P, _P, _P, _P, _P, _L, _I, _I, _I, _I, _F, _P]),
     'mica_selftest_wait_timeout': (_I, [_P, _I, _P]),

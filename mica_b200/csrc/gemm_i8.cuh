@@ -64,6 +64,7 @@ struct GemmArgs {
     int8_t* q_out;        // [M, I]
     long ldq;
     float* s_out;         // [M]
+    const float* inv_h;   // [I] or nullptr: down_proj's inv_smooth, applied before the requant
 };
 
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
@@ -79,6 +80,15 @@ __device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(_
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
     asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d)
                  : "memory");
+}
+
+// f[e] = RN(f[e] * inv[e]) for eight consecutive columns (inv 16-byte aligned).
+__device__ __forceinline__ void scale8(float (&f)[8], const float* inv) {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(inv));
+    const float4 b = __ldg(reinterpret_cast<const float4*>(inv) + 1);
+    const float iv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+    for (int e = 0; e < 8; ++e) f[e] = __fmul_rn(f[e], iv[e]);
 }
 
 // Phase 2 of the fused SwiGLU kernel: each warp requantises whole rows of h [M, N/2] with
@@ -107,6 +117,10 @@ __device__ __forceinline__ void swiglu_requant_rows(const GemmArgs& args, int wa
                 f0[2 * j + 1] = __uint_as_float(w0[j] & 0xFFFF0000u);
                 f1[2 * j] = __uint_as_float(w1[j] << 16);
                 f1[2 * j + 1] = __uint_as_float(w1[j] & 0xFFFF0000u);
+            }
+            if (args.inv_h != nullptr) {
+                scale8(f0, args.inv_h + c);
+                if (has2) scale8(f1, args.inv_h + c2);
             }
             *reinterpret_cast<uint2*>(qrow + c) = quant8<MODE>(f0, scale, rscale);
             if (has2) *reinterpret_cast<uint2*>(qrow + c2) = quant8<MODE>(f1, scale, rscale);
@@ -354,6 +368,9 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
                         const int gcol = n0 + col0 + lane;
                         const float sb_l = gcol < N ? args.sb[gcol] : 0.f;
                         const float bias_l = (args.bias != nullptr && gcol < N) ? args.bias[gcol] : 0.f;
+                        // down_proj's smoothing of h column (n0 + col0) / 2 + (lane & 15)
+                        const int hcol = (n0 + col0) / 2 + (lane & 15);
+                        const float inv_l = (args.inv_h != nullptr && hcol < N / 2) ? args.inv_h[hcol] : 1.f;
                         uint32_t r[32];
                         tmem_ld_32x32b_x32(t_row + col0, r);
                         tmem_ld_wait();
@@ -379,7 +396,10 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
                                 // chains of a chunk interleave instead of serialising on slow paths
                                 const float act = bf16_round(__fdividef(g, 1.0f + __expf(-g)));
                                 const float h = bf16_round(__fmul_rn(act, u));
-                                amax = fmaxf(amax, fabsf(h));
+                                // the requant's input is RN(h * inv) (act_quant's xf * inv_smooth)
+                                const float hs = args.inv_h != nullptr
+                                                     ? __fmul_rn(h, __shfl_sync(0xffffffffu, inv_l, jj)) : h;
+                                amax = fmaxf(amax, fabsf(hs));
                                 hv[e] = h;
                             }
                             p[j / 2] = pack_bf16(hv[0], hv[1]);

@@ -316,22 +316,24 @@ int mica_device_error(int* code, void* stream) {
 }
 
 // ---------------------------------------------------------------------------------------
-static int quant_launch(const QuantArgs& a, int dtype, bool norm, cudaStream_t st) {
+static int quant_launch(const QuantArgs& a, int dtype, int kind, cudaStream_t st) {
     const int nvec = a.K / 8;
     int threads = ((nvec + QV - 1) / QV + 31) / 32 * 32;
     if (threads < 32) threads = 32;
     if (threads > 1024) return MICA_ERR_UNSUPPORTED;
     const dim3 grid(a.M), block(threads);
-    if (norm && dtype == MICA_DT_FP32) return MICA_ERR_ARG;
+    if (kind != QK_PLAIN && dtype == MICA_DT_FP32) return MICA_ERR_ARG;
+#define QLAUNCH_T(T, MAXT)                                                                    \
+    if (kind == QK_NORM) quant_rows_kernel<T, QK_NORM, MAXT><<<grid, block, 0, st>>>(a);      \
+    else if (kind == QK_SWIGLU) quant_rows_kernel<T, QK_SWIGLU, MAXT><<<grid, block, 0, st>>>(a); \
+    else quant_rows_kernel<T, QK_PLAIN, MAXT><<<grid, block, 0, st>>>(a);
 #define QLAUNCH(MAXT)                                                                         \
     if (dtype == MICA_DT_BF16) {                                                              \
-        if (norm) quant_rows_kernel<__nv_bfloat16, true, MAXT><<<grid, block, 0, st>>>(a);    \
-        else quant_rows_kernel<__nv_bfloat16, false, MAXT><<<grid, block, 0, st>>>(a);       \
+        QLAUNCH_T(__nv_bfloat16, MAXT)                                                        \
     } else if (dtype == MICA_DT_FP16) {                                                       \
-        if (norm) quant_rows_kernel<__half, true, MAXT><<<grid, block, 0, st>>>(a);           \
-        else quant_rows_kernel<__half, false, MAXT><<<grid, block, 0, st>>>(a);              \
+        QLAUNCH_T(__half, MAXT)                                                               \
     } else {                                                                                  \
-        quant_rows_kernel<float, false, MAXT><<<grid, block, 0, st>>>(a);                     \
+        quant_rows_kernel<float, QK_PLAIN, MAXT><<<grid, block, 0, st>>>(a);                  \
     }
     if (threads <= 512) {
         QLAUNCH(512)
@@ -339,6 +341,7 @@ static int quant_launch(const QuantArgs& a, int dtype, bool norm, cudaStream_t s
         QLAUNCH(1024)
     }
 #undef QLAUNCH
+#undef QLAUNCH_T
     return launch_status();
 }
 
@@ -355,7 +358,7 @@ int mica_act_quant(const void* x, int x_dtype, long ldx, const float* inv, int8_
     QuantArgs a = {};
     a.x = x; a.ldx = ldx; a.inv = inv; a.q = q; a.ldq = ldq; a.s = s;
     a.M = M; a.K = K; a.round_mode = round_mode;
-    return quant_launch(a, x_dtype, false, static_cast<cudaStream_t>(stream));
+    return quant_launch(a, x_dtype, QK_PLAIN, static_cast<cudaStream_t>(stream));
 }
 
 int mica_rmsnorm_quant(const void* x, int x_dtype, long ldx, const void* residual, long ldr, const void* gamma,
@@ -380,7 +383,7 @@ int mica_rmsnorm_quant(const void* x, int x_dtype, long ldx, const void* residua
     a.x = x; a.ldx = ldx; a.residual = residual; a.ldr = ldr; a.gamma = gamma; a.norm_style = norm_style;
     a.eps = eps; a.inv = inv; a.y_out = y_out; a.ldy = ldy; a.sum_out = sum_out; a.ldsum = ldsum;
     a.q = q; a.ldq = ldq; a.s = s; a.M = M; a.K = K; a.round_mode = round_mode;
-    return quant_launch(a, x_dtype, true, static_cast<cudaStream_t>(stream));
+    return quant_launch(a, x_dtype, QK_NORM, static_cast<cudaStream_t>(stream));
 }
 
 // ---------------------------------------------------------------------------------------
@@ -472,16 +475,16 @@ size_t mica_swiglu_workspace_bytes(int M) {
 }
 
 int mica_w8a8_gemm_swiglu_quant(const int8_t* A, long lda, const int8_t* Bgu, long ldb, const float* sa,
-                                const float* sgu, const float* bias_gu, void* h_out, long ldh, int8_t* q_out, long ldq,
-                                float* s_out, int M, int I, int K, int round_mode, void* workspace,
-                                size_t workspace_bytes, void* stream) {
+                                const float* sgu, const float* bias_gu, const float* inv_h, void* h_out, long ldh,
+                                int8_t* q_out, long ldq, float* s_out, int M, int I, int K, int round_mode,
+                                void* workspace, size_t workspace_bytes, void* stream) {
     if (!A || !Bgu || !sa || !sgu || !h_out || !q_out || !s_out || (round_mode != 0 && round_mode != 1))
         return MICA_ERR_ARG;
     if (M < 0 || I < 16 || (I & 15) || K < 16 || (K & 15) || lda < K || ldb < K || ldh < I || ldq < I)
         return MICA_ERR_SHAPE;
     if (M > (1 << 30) || I > (1 << 29) || K > (1 << 30)) return MICA_ERR_RANGE;
     if (!aligned16(A) || !aligned16(Bgu) || !aligned16(h_out) || !aligned16(q_out) || lda % 16 || ldb % 16 ||
-        (ldh * 2) % 16 || ldq % 16)
+        (ldh * 2) % 16 || ldq % 16 || (inv_h && !aligned16(inv_h)))
         return MICA_ERR_ALIGN;
     if (!workspace || !aligned16(workspace)) return workspace ? MICA_ERR_ALIGN : MICA_ERR_ARG;
     if (workspace_bytes < mica_swiglu_workspace_bytes(M)) return MICA_ERR_WORKSPACE;
@@ -506,6 +509,7 @@ int mica_w8a8_gemm_swiglu_quant(const int8_t* A, long lda, const int8_t* Bgu, lo
     g.sa = sa; g.sb = sgu; g.bias = bias_gu; g.M = M; g.N = N; g.K = K; g.round_mode = round_mode;
     g.row_amax = amax; g.grid_sync = sync;
     g.h = static_cast<const __nv_bfloat16*>(h_out); g.ldh = ldh; g.q_out = q_out; g.ldq = ldq; g.s_out = s_out;
+    g.inv_h = inv_h;
     const long tiles = static_cast<long>((M + 127) / 128) * ((N + bn - 1) / bn);
     const int grid = static_cast<int>(tiles < sms ? tiles : sms);
     if (bn == 256) return gemm_launch<256, EPI_SWIGLU, __nv_bfloat16, 8>(ta, tb, th, g, grid, true, st);
@@ -548,8 +552,8 @@ static int noalloc_scratch(void** out) {
 }
 
 int mica_w8a8_gemm_swiglu_quant_noalloc(const int8_t* A, long lda, const int8_t* Bgu, long ldb, const float* sa,
-                                        const float* sgu, const float* bias_gu, void* h_out, long ldh,
-                                        int8_t* q_out, long ldq, float* s_out, int M, int I, int K,
+                                        const float* sgu, const float* bias_gu, const float* inv_h, void* h_out,
+                                        long ldh, int8_t* q_out, long ldq, float* s_out, int M, int I, int K,
                                         int round_mode, void* stream) {
     if (M > MICA_NOALLOC_MAX_ROWS) return MICA_ERR_WORKSPACE;   // beyond the fixed scratch: refuse up front
     int rc = check_device(nullptr);
@@ -558,8 +562,31 @@ int mica_w8a8_gemm_swiglu_quant_noalloc(const int8_t* A, long lda, const int8_t*
     if ((rc = noalloc_scratch(&scratch))) return rc;
     // The shared entry point clears the rows it uses (cudaMemsetAsync, no allocation)
     // before launching, so stale contents from the previous call do not leak in.
-    return mica_w8a8_gemm_swiglu_quant(A, lda, Bgu, ldb, sa, sgu, bias_gu, h_out, ldh, q_out, ldq, s_out, M, I, K,
-                                       round_mode, scratch, MICA_NOALLOC_SCRATCH_BYTES, stream);
+    return mica_w8a8_gemm_swiglu_quant(A, lda, Bgu, ldb, sa, sgu, bias_gu, inv_h, h_out, ldh, q_out, ldq, s_out, M,
+                                       I, K, round_mode, scratch, MICA_NOALLOC_SCRATCH_BYTES, stream);
+}
+
+// ---------------------------------------------------------------------------------------
+int mica_swiglu_quant(const void* g, long ldg, const void* u, long ldu, int dtype, const float* inv, void* h_out,
+                      long ldh, int8_t* q, long ldq, float* s, int M, int I, int round_mode, void* stream) {
+    if (!g || !u || (!q != !s) || (!q && !h_out) || (dtype != MICA_DT_BF16 && dtype != MICA_DT_FP16) ||
+        (round_mode != 0 && round_mode != 1))
+        return MICA_ERR_ARG;
+    if (M < 0 || I < 8 || (I & 7) || ldg < I || ldu < I || (h_out && ldh < I) || (q && ldq < I))
+        return MICA_ERR_SHAPE;
+    const long ld_max = std::max(std::max(ldg, ldu), std::max(h_out ? ldh : 0L, q ? ldq : 0L));
+    if (static_cast<long>(M) * ld_max >= (1L << 40)) return MICA_ERR_RANGE;
+    if (!aligned16(g) || !aligned16(u) || (h_out && !aligned16(h_out)) || (q && !aligned16(q)) ||
+        (inv && !aligned16(inv)) || (ldg * 2) % 16 || (ldu * 2) % 16 || (h_out && (ldh * 2) % 16) ||
+        (q && ldq % 16))
+        return MICA_ERR_ALIGN;
+    int rc = check_device(nullptr);
+    if (rc) return rc;
+    if (M == 0) return MICA_OK;
+    QuantArgs a = {};
+    a.x = g; a.ldx = ldg; a.residual = u; a.ldr = ldu; a.inv = inv; a.y_out = h_out; a.ldy = ldh;
+    a.q = q; a.ldq = ldq; a.s = s; a.M = M; a.K = I; a.round_mode = round_mode;
+    return quant_launch(a, dtype, QK_SWIGLU, static_cast<cudaStream_t>(stream));
 }
 
 // ---------------------------------------------------------------------------------------

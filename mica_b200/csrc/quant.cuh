@@ -176,12 +176,20 @@ __device__ __forceinline__ void quant_row_packed(const QuantArgs& a, float* red)
     if (threadIdx.x == 0) a.s[row] = scale;
 }
 
-// NORM = false: mica_act_quant. NORM = true: mica_rmsnorm_quant. MAXT bounds the block
-// size (512 for rows up to 16384 elements, 1024 beyond), which bounds registers per thread.
-template <typename T, bool NORM, int MAXT = 512>
+// What a row goes through before the quantiser.
+enum QuantKind {
+    QK_PLAIN = 0,    // mica_act_quant: x as is
+    QK_NORM = 1,     // mica_rmsnorm_quant: residual add, RMSNorm
+    QK_SWIGLU = 2,   // mica_swiglu_quant: h = RN(RN(silu(g)) * u) with g = x, u = residual
+};
+
+// MAXT bounds the block size (512 for rows up to 16384 elements, 1024 beyond), which bounds
+// registers per thread.
+template <typename T, int KIND, int MAXT = 512>
 __global__ void __launch_bounds__(MAXT) quant_rows_kernel(const QuantArgs a) {
+    constexpr bool NORM = KIND == QK_NORM;
     __shared__ float red[32];
-    if constexpr (!NORM && sizeof(T) == 2) {
+    if constexpr (KIND == QK_PLAIN && sizeof(T) == 2) {
         if (a.inv == nullptr) {
             if (a.round_mode == MICA_ROUND_HALF_EVEN) quant_row_packed<T, MICA_ROUND_HALF_EVEN>(a, red);
             else quant_row_packed<T, MICA_ROUND_HALF_AWAY>(a, red);
@@ -245,7 +253,29 @@ __global__ void __launch_bounds__(MAXT) quant_rows_kernel(const QuantArgs a) {
         }
     }
 
-    if (NORM && a.q == nullptr) return;  // norm-only call (fused_kernels.rms_norm drop-in)
+    if constexpr (KIND == QK_SWIGLU) {
+        // fused_kernels.swiglu (lib/fused_kernels.py:37-44): silu in fp32 rounded to the
+        // activation dtype, times u, rounded again; silu as in the fused GEMM epilogue.
+        const T* ur = static_cast<const T*>(a.residual) + static_cast<long>(row) * a.ldr;
+#pragma unroll
+        for (int i = 0; i < QV; ++i) {
+            const int idx = threadIdx.x + i * blockDim.x;
+            if (idx < nvec) {
+                float u[8];
+                load8(ur + idx * 8, u);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    const float g = v[i][e];
+                    const float act = round_to<T>(__fdividef(g, 1.0f + __expf(-g)));
+                    v[i][e] = round_to<T>(__fmul_rn(act, u[e]));
+                }
+                if (a.y_out != nullptr)
+                    store8(static_cast<T*>(a.y_out) + static_cast<long>(row) * a.ldy + idx * 8, v[i]);
+            }
+        }
+    }
+
+    if (KIND != QK_PLAIN && a.q == nullptr) return;  // norm-only / swiglu-only call
     if (a.inv != nullptr) {
 #pragma unroll
         for (int i = 0; i < QV; ++i) {

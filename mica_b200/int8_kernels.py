@@ -11,7 +11,8 @@ STATS['fallback'] (:19-24), so QLinear's own fallback logic is unchanged. Hard e
 (CUDA failures) raise. Unlike the reference, no cubin container is read: the kernels
 live in libmica_w8a8.so, built from csrc/ for sm_100a.
 
-Additions used by the fused paths: rmsnorm_quant, mm_i8_swiglu_quant, option_logits.
+Additions used by the fused paths: rmsnorm_quant, mm_i8_swiglu_quant, swiglu_quant / swi_glu,
+option_logits.
 """
 from __future__ import annotations
 
@@ -100,7 +101,7 @@ def _round_code():
 
 
 def _aligned(*ts):
-    return all(t.data_ptr() % 16 == 0 for t in ts)
+    return all(t.data_ptr() % 16 == 0 for t in ts if t is not None)
 
 
 def _supported(dev):
@@ -184,23 +185,54 @@ def rmsnorm_quant(x, weight, eps, residual=None, inv_smooth=None, style=N.NORM_O
     return r
 
 
-def mm_i8_swiglu_quant(qx, sx, qw_gu, sw_gu, bias=None):
+def mm_i8_swiglu_quant(qx, sx, qw_gu, sw_gu, bias=None, inv_h=None):
     """gate_up GEMM + SwiGLU + per-token requantisation of the product (one kernel).
 
     qw_gu/sw_gu hold gate and up rows interleaved in groups of 16 (int8_runtime.interleave_gate_up).
+    inv_h [I] is down_proj's inv_smooth (the requantisation quantises h * inv_h), or None.
     Returns (h bf16 [M, I], q int8 [M, I], s fp32 [M])."""
     if qx.dim() != 2 or qx.dtype != torch.int8 or qw_gu.dtype != torch.int8 or qw_gu.shape[0] % 32:
         return _miss('swiglu_input')
     m, k = qx.shape
     if qw_gu.shape[1] != k or not qx.is_contiguous() or not qw_gu.is_contiguous():
         return _miss('swiglu_contiguous')
-    if k % 16 or not _aligned(qx, qw_gu):
+    if inv_h is not None and (inv_h.dtype != torch.float32 or inv_h.numel() != qw_gu.shape[0] // 2):
+        return _miss('act_inv')
+    if k % 16 or not _aligned(qx, qw_gu, inv_h):
         return _miss('align')
     if not _supported(qx.device):
         return _miss('no_container')
-    r = torch.ops.mica.gemm_swiglu_quant(qx, sx, qw_gu, sw_gu, bias, _round_code())
+    r = torch.ops.mica.gemm_swiglu_quant(qx, sx, qw_gu, sw_gu, bias, inv_h, _round_code())
     _launched()
     return r
+
+
+def swiglu_quant(gate, up, inv=None, want_h=False, want_q=True):
+    """h = bf16(bf16(silu(gate)) * up) (fused_kernels.swi_glu, lib/fused_kernels.py:85-96), then
+    down_proj's per-token quantisation of h * inv (one kernel). For MLPs whose gate and up
+    projections quantise their input differently. Returns (h, q, s); h is empty unless
+    want_h, q/s are empty unless want_q."""
+    if gate.dim() != 2 or gate.shape != up.shape or gate.dtype != up.dtype or gate.dtype not in (
+            torch.bfloat16, torch.float16) or gate.device.type != 'cuda':
+        return _miss('swiglu_input')
+    m, i = gate.shape
+    if gate.stride(1) != 1 or up.stride(1) != 1:
+        return _miss('swiglu_contiguous')
+    if inv is not None and (inv.dtype != torch.float32 or inv.numel() != i):
+        return _miss('act_inv')
+    if i % 8 or (gate.stride(0) * 2) % 16 or (up.stride(0) * 2) % 16 or not _aligned(gate, up, inv):
+        return _miss('align')
+    if not _supported(gate.device):
+        return _miss('no_container')
+    r = torch.ops.mica.swiglu_quant(gate, up, inv, _round_code(), bool(want_h), bool(want_q))
+    _launched()
+    return r
+
+
+def swi_glu(gate, up):
+    """fused_kernels.swi_glu drop-in (lib/fused_kernels.py:85-96): bf16(bf16(silu(gate)) * up)."""
+    r = swiglu_quant(gate, up, None, want_h=True, want_q=False)
+    return None if r is None else r[0]
 
 
 def option_logits(h, rows, gamma=None, lo=None, hi=None, eps=1e-6, style=N.NORM_WEIGHT):

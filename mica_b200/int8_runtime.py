@@ -160,6 +160,13 @@ class QLinear(nn.Module):
         return y.reshape(*shape[:-1], self.out_features)
 
 
+def same_smoothing(a, b) -> bool:
+    """True when two projections quantise their (shared) input identically."""
+    if a is None or b is None:
+        return a is None and b is None
+    return a.shape == b.shape and bool(torch.equal(a, b))
+
+
 def interleave_gate_up(gate: torch.Tensor, up: torch.Tensor, group: int = 16) -> torch.Tensor:
     """Fused gate_up row order: `group` gate rows, then the same `group` up rows, repeated
     (what the SwiGLU epilogue of mica_w8a8_gemm_swiglu_quant expects). [I, ...] -> [2I, ...]."""
@@ -172,25 +179,30 @@ def interleave_gate_up(gate: torch.Tensor, up: torch.Tensor, group: int = 16) ->
 
 
 class FusedMLP(nn.Module):
-    """SwiGLU MLP as two kernels: [gate|up] GEMM + SwiGLU + requant, then the down GEMM.
+    """SwiGLU MLP (the reference's fast_runtime._fused_mlp, lib/fast_runtime.py:126-132).
+
+    When gate_proj and up_proj share their input quantisation (no smoothing, or the same
+    inv_smooth) it runs as two kernels: [gate|up] GEMM + SwiGLU + requantisation, then the
+    down GEMM. When their smoothing differs (per-projection smoothing, as the reference's
+    convert produces) it runs gate and up as separate QLinear GEMMs, then one SwiGLU +
+    requantisation kernel, then the down GEMM. down_proj's smoothing is applied inside the
+    requantisation either way.
 
     Built from a module with gate_proj / up_proj / down_proj Linears (HF Qwen3MLP) or from
-    existing QLinears. Smoothing vectors must be absent or shared by gate and up (one
-    quantisation of x feeds both); down_proj's own smoothing is not supported here
-    because its input is quantised inside the gate_up kernel."""
+    existing QLinears."""
 
     def __init__(self, mlp, stats=None, prefix='', alpha=ALPHA):
         super().__init__()
         g, u, d = mlp.gate_proj, mlp.up_proj, mlp.down_proj
         get = (lambda name: stats.get(prefix + name)) if stats is not None else (lambda name: None)
+        self.split = None
         if isinstance(g, QLinear):
             qg, sg, qu, su, inv = g.qweight, g.wscale, u.qweight, u.wscale, g.inv_smooth
-            if (g.inv_smooth is None) != (u.inv_smooth is None) or (
-                    g.inv_smooth is not None and not torch.equal(g.inv_smooth, u.inv_smooth)):
-                raise ValueError('gate_proj and up_proj need the same smoothing to share one quantisation')
             bg, bu = g.bias, u.bias
             self.down = d if isinstance(d, QLinear) else QLinear(d)
             self.out_dtype = g.out_dtype
+            if not same_smoothing(g.inv_smooth, u.inv_smooth):
+                self.split = nn.ModuleList([g, u])      # two quantisations of x: no shared operand
         else:
             amax = get('gate_proj')
             smooth = None
@@ -207,9 +219,10 @@ class FusedMLP(nn.Module):
             bu = None if u.bias is None else u.bias.detach().float()
             self.down = QLinear(d)
             self.out_dtype = g.weight.dtype
-        if self.down.inv_smooth is not None:
-            raise ValueError('down_proj smoothing is not supported by the fused MLP')
         self.inner = qg.shape[0]
+        if self.split is not None:
+            self.inv_smooth = self.qweight_gu = self.wscale_gu = self.bias_gu = None
+            return
         self.register_buffer('inv_smooth', inv)
         self.register_buffer('qweight_gu', interleave_gate_up(qg, qu))
         self.register_buffer('wscale_gu', interleave_gate_up(sg, su))
@@ -224,11 +237,14 @@ class FusedMLP(nn.Module):
         return r
 
     def forward_quantised(self, qx, sx):
+        """Shared-quantisation path: [gate|up] + SwiGLU + requant, then down."""
         before = dict(aot.STATS['fallback'])
-        r = aot.mm_i8_swiglu_quant(qx, sx, self.qweight_gu, self.wscale_gu, self.bias_gu)
+        r = aot.mm_i8_swiglu_quant(qx, sx, self.qweight_gu, self.wscale_gu, self.bias_gu, self.down.inv_smooth)
         if r is None:
             raise KernelMiss(f'gate_up miss ({_last_miss(before)})')
-        _, qh, sh = r
+        return self._down(r[1], r[2], before)
+
+    def _down(self, qh, sh, before):
         y = aot.mm_i8(qh, sh, self.down.qweight, self.down.wscale, self.down.bias, self.out_dtype)
         if y is None:
             raise KernelMiss(f'down_proj miss ({_last_miss(before)})')
@@ -239,8 +255,69 @@ class FusedMLP(nn.Module):
         x2 = x.reshape(-1, shape[-1])
         if x2.shape[0] == 0:
             return x.new_zeros(*shape[:-1], self.down.out_features, dtype=self.out_dtype)
-        qx, sx = self.quantise_input(x2)
-        return self.forward_quantised(qx, sx).reshape(*shape[:-1], self.down.out_features)
+        if self.split is not None:
+            before = dict(aot.STATS['fallback'])
+            g, u = (lin(x2) for lin in self.split)
+            r = aot.swiglu_quant(g, u, self.down.inv_smooth)
+            if r is None:
+                raise KernelMiss(f'swiglu miss ({_last_miss(before)})')
+            y = self._down(r[1], r[2], before)
+        else:
+            qx, sx = self.quantise_input(x2)
+            y = self.forward_quantised(qx, sx)
+        return y.reshape(*shape[:-1], self.down.out_features)
+
+
+# ---------------------------------------------------------------------------------------
+# INT8 weights file (lib/int8_runtime.py:639-726): a safetensors file whose metadata holds
+# format = FILE_FORMAT and `ties` (JSON {alias: source}) for tensors stored once; the keys are
+# the model's state dict with every converted projection's QLinear buffers (qweight int8
+# [N, K], wscale fp32 [N], and inv_smooth fp32 [K] / bias fp32 [N] when present).
+FILE = 'model-int8.safetensors'
+FILE_FORMAT = 'int8-w8a8/1'
+
+
+class InvalidModel(ValueError):
+    """The reference's ValueError('invalid_model'), with the reason appended."""
+
+    def __init__(self, why):
+        super().__init__(f'invalid_model: {why}')
+
+
+def read_int8_file(path, device='cpu'):
+    """Reads an int8-w8a8/1 file (a folder holding FILE, or the file itself).
+
+    Returns (tensors, ties): every stored tensor by key, with each tied alias resolved to its
+    source tensor (the same object), and the ties map. Raises InvalidModel on a wrong format
+    tag or a tie whose source is missing (lib/int8_runtime.py:679-688)."""
+    import json
+    from pathlib import Path
+    from safetensors import safe_open
+    path = Path(path)
+    if path.is_dir():
+        path = path / FILE
+    with safe_open(str(path), framework='pt', device=str(device)) as f:
+        meta = f.metadata() or {}
+        if meta.get('format') != FILE_FORMAT:
+            raise InvalidModel(f"format {meta.get('format')!r}, expected {FILE_FORMAT!r}")
+        ties = json.loads(meta.get('ties') or '{}')
+        keys = set(f.keys())
+        bad = [a for a, src in ties.items() if src not in keys or a in keys]
+        if bad:
+            raise InvalidModel(f'ties without a stored source: {sorted(bad)[:4]}')
+        tensors = {k: f.get_tensor(k) for k in sorted(keys)}
+    for alias, src in ties.items():
+        tensors[alias] = tensors[src]
+    return tensors, ties
+
+
+def write_int8_file(path, tensors: dict, ties: dict | None = None):
+    """Writes tensors (tied aliases left out: pass them in `ties`) as an int8-w8a8/1 file."""
+    import json
+    from safetensors.torch import save_file
+    ties = dict(ties or {})
+    stored = {k: v.contiguous() for k, v in tensors.items() if k not in ties}
+    save_file(stored, str(path), metadata={'format': FILE_FORMAT, 'ties': json.dumps(ties, sort_keys=True)})
 
 
 def target_linears(body, layers=None, modules=None):

@@ -10,7 +10,9 @@ shapes without running anything.
     torch.ops.mica.rmsnorm_quant(x, residual, gamma, inv, eps, style, round_mode, want_y)
                                                                         -> (q, s, y, sum)
     torch.ops.mica.w8a8_gemm(qx, sx, qw, sw, bias, out_dtype, tile)     -> y
-    torch.ops.mica.gemm_swiglu_quant(qx, sx, qw_gu, sw_gu, bias, round_mode) -> (h, q, s)
+    torch.ops.mica.w8a8_gemm_into(qx, sx, qw, sw, bias, out, tile)      (writes out, a row-strided view)
+    torch.ops.mica.gemm_swiglu_quant(qx, sx, qw_gu, sw_gu, bias, inv_h, round_mode) -> (h, q, s)
+    torch.ops.mica.swiglu_quant(g, u, inv, round_mode, want_h, want_q) -> (h, q, s)
     torch.ops.mica.option_logits(h, rows, gamma, lo, hi, eps, style)    -> (logits, probs)
     torch.ops.mica.qk_norm_rope(qkv, q_w, k_w, cos, sin, pos, pos0, heads, kv_heads, eps)  (in place)
 """
@@ -119,10 +121,32 @@ def _(qx, sx, qw, sw, bias, out_dtype, tile):
     return qx.new_empty((qx.shape[0], qw.shape[0]), dtype=OUT_DTYPES[out_dtype])
 
 
+_OUT_CODE = {torch.bfloat16: 0, torch.float16: 1, torch.float32: 2}
+
+
+@torch.library.custom_op('mica::w8a8_gemm_into', mutates_args=('out',))
+def w8a8_gemm_into(qx: torch.Tensor, sx: torch.Tensor, qw: torch.Tensor, sw: torch.Tensor,
+                   bias: Optional[torch.Tensor], out: torch.Tensor, tile: int) -> None:
+    """As w8a8_gemm, writing into `out` [M, N] (unit column stride, any row stride): e.g. the
+    q, k and v slices of one qkv buffer when the three projections quantise their input
+    differently."""
+    m, k = qx.shape
+    n = qw.shape[0]
+    with _on(qx):
+        N.call('mica_w8a8_gemm_cfg', qx.data_ptr(), qx.stride(0), qw.data_ptr(), qw.stride(0), sx.data_ptr(),
+               sw.data_ptr(), _ptr(bias), out.data_ptr(), _OUT_CODE[out.dtype], out.stride(0), m, n, k, tile // 1000,
+               tile % 1000, 0, _stream(qx))
+
+
+@w8a8_gemm_into.register_fake
+def _(qx, sx, qw, sw, bias, out, tile):
+    return None
+
+
 # ---------------------------------------------------------------------------------------
 @torch.library.custom_op('mica::gemm_swiglu_quant', mutates_args=())
 def gemm_swiglu_quant(qx: torch.Tensor, sx: torch.Tensor, qw_gu: torch.Tensor, sw_gu: torch.Tensor,
-                      bias: Optional[torch.Tensor], round_mode: int
+                      bias: Optional[torch.Tensor], inv_h: Optional[torch.Tensor], round_mode: int
                       ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
     m, k = qx.shape
     i = qw_gu.shape[0] // 2
@@ -134,16 +158,40 @@ def gemm_swiglu_quant(qx: torch.Tensor, sx: torch.Tensor, qw_gu: torch.Tensor, s
     ws = torch.empty((max(ws_bytes, 16),), dtype=torch.uint8, device=dev)
     with _on(qx):
         N.call('mica_w8a8_gemm_swiglu_quant', qx.data_ptr(), qx.stride(0), qw_gu.data_ptr(), qw_gu.stride(0),
-               sx.data_ptr(), sw_gu.data_ptr(), _ptr(bias), h.data_ptr(), h.stride(0), q.data_ptr(), q.stride(0),
+               sx.data_ptr(), sw_gu.data_ptr(), _ptr(bias), _ptr(inv_h), h.data_ptr(), h.stride(0), q.data_ptr(),
+               q.stride(0),
                s.data_ptr(), m, i, k, round_mode, ws.data_ptr(), ws.numel(), _stream(qx))
     return h, q, s
 
 
 @gemm_swiglu_quant.register_fake
-def _(qx, sx, qw_gu, sw_gu, bias, round_mode):
+def _(qx, sx, qw_gu, sw_gu, bias, inv_h, round_mode):
     m, i = qx.shape[0], qw_gu.shape[0] // 2
     return (qx.new_empty((m, i), dtype=torch.bfloat16), qx.new_empty((m, i), dtype=torch.int8),
             qx.new_empty((m,), dtype=torch.float32))
+
+
+# ---------------------------------------------------------------------------------------
+@torch.library.custom_op('mica::swiglu_quant', mutates_args=())
+def swiglu_quant(g: torch.Tensor, u: torch.Tensor, inv: Optional[torch.Tensor], round_mode: int, want_h: bool,
+                 want_q: bool) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    m, i = g.shape
+    dev = g.device
+    h = torch.empty((m, i) if want_h else (0,), dtype=g.dtype, device=dev)
+    q = torch.empty((m, i) if want_q else (0,), dtype=torch.int8, device=dev)
+    s = torch.empty((m,) if want_q else (0,), dtype=torch.float32, device=dev)
+    with _on(g):
+        N.call('mica_swiglu_quant', g.data_ptr(), g.stride(0), u.data_ptr(), u.stride(0), DTYPE_CODE[g.dtype],
+               _ptr(inv), h.data_ptr() if want_h else None, i if want_h else 0, q.data_ptr() if want_q else None,
+               i if want_q else 0, s.data_ptr() if want_q else None, m, i, round_mode, _stream(g))
+    return h, q, s
+
+
+@swiglu_quant.register_fake
+def _(g, u, inv, round_mode, want_h, want_q):
+    m, i = g.shape
+    return (g.new_empty((m, i) if want_h else (0,)), g.new_empty((m, i) if want_q else (0,), dtype=torch.int8),
+            g.new_empty((m,) if want_q else (0,), dtype=torch.float32))
 
 
 # ---------------------------------------------------------------------------------------

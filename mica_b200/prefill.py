@@ -5,14 +5,18 @@ PrefillEngine does for one request (v0.5/serving/lib/prefill_engine.py:274-339 r
 final_hidden, :385-418 capture / replay) on the dense decoder of BASELINE configs 3-4
 (Qwen3-4B dims: hidden 2560, 32 q / 8 kv heads x 128, FFN 9728, 36 layers).
 
-Per layer, five launches of this library plus attention:
+Per layer, seven launches of this library plus attention:
   rmsnorm_quant(prev_out, residual)  -> new residual stream + int8 codes (fused prologue)
-  w8a8 GEMM QKV (tcgen05)            -> q, k, v  (q/k RMSNorm + RoPE in torch, bf16, as HF)
+  w8a8 GEMM QKV (tcgen05)            -> q, k, v
+  qk_norm_rope                       -> q/k RMSNorm + RoPE in place (the HF op sequence)
   attention: torch SDPA (cuDNN/flash), causal, GQA
   act_quant(attn) + w8a8 GEMM O
   rmsnorm_quant(o, residual)         -> codes for the MLP
   gate_up GEMM + SwiGLU + requant    -> codes for down (one cooperative launch)
   w8a8 GEMM down
+Models with per-projection smoothing (an int8-w8a8/1 file, load_model) quantise a block's
+normed input once per distinct smoothing vector and, when gate and up differ, run them as
+two GEMMs plus one SwiGLU + requant kernel.
 The last layer computes K/V for every row but Q, attention, O and the MLP only for the
 scored row (prefill_engine.py:306-339), then the fused final norm + gathered lm_head GEMV
 + option softmax (release_runtime.py:302-306, :509-522).
@@ -31,7 +35,7 @@ import torch.nn.functional as F
 from . import _native as N
 from . import int8_kernels as K
 from . import ops  # noqa: F401
-from .int8_runtime import interleave_gate_up, quant_weight
+from .int8_runtime import InvalidModel, interleave_gate_up, quant_weight, read_int8_file
 
 BUCKET = 64            # graph buckets (the reference's 64-token buckets)
 EAGER_BUCKET = 256     # padding granularity of eager (uncaptured) requests
@@ -61,6 +65,15 @@ class DecoderConfig:
 
 @dataclass
 class Layer:
+    """One decoder layer's weights. int8 weights [N, K] with fp32 channel scales [N];
+    optional fp32 biases [N] and smoothing vectors inv_smooth [K] (the reference QLinear's
+    buffers, lib/int8_runtime.py:108-127).
+
+    q/k/v are stacked into qkv_w. qkv_parts lists the row ranges (lo, hi, inv) that share one
+    input quantisation: one part when the three projections quantise x alike (no smoothing,
+    or the same inv_smooth), else one part per projection. The MLP is fused (gu_w/gu_s:
+    gate and up rows interleaved by interleave_gate_up, sharing inv gu_inv) or, when gate and
+    up are smoothed differently, split (g_* and u_* kept apart)."""
     in_norm: torch.Tensor
     qkv_w: torch.Tensor
     qkv_s: torch.Tensor
@@ -73,6 +86,32 @@ class Layer:
     gu_s: torch.Tensor
     down_w: torch.Tensor
     down_s: torch.Tensor
+    qkv_b: torch.Tensor = None
+    qkv_parts: list = None          # [(lo, hi, inv or None)]; None = one part, no smoothing
+    o_inv: torch.Tensor = None
+    o_b: torch.Tensor = None
+    gu_inv: torch.Tensor = None
+    gu_b: torch.Tensor = None
+    split_mlp: tuple = None         # (g_w, g_s, g_inv, g_b, u_w, u_s, u_inv, u_b) when gu_w is None
+    down_inv: torch.Tensor = None
+    down_b: torch.Tensor = None
+
+    def parts(self):
+        return self.qkv_parts if self.qkv_parts is not None else [(0, self.qkv_w.shape[0], None)]
+
+    def mlp_in_inv(self):
+        """Smoothing of the MLP's first quantisation (gate's when split)."""
+        return self.split_mlp[2] if self.split_mlp is not None else self.gu_inv
+
+    def distinct_attn_invs(self) -> int:
+        return len({_inv_key(inv) for _, _, inv in self.parts()})
+
+    def distinct_mlp_invs(self) -> int:
+        return 1 if self.split_mlp is None else len({_inv_key(self.split_mlp[2]), _inv_key(self.split_mlp[6])})
+
+
+def _inv_key(inv):
+    return None if inv is None else inv.data_ptr()
 
 
 @dataclass
@@ -125,6 +164,143 @@ def from_hf_state(state: dict, cfg: DecoderConfig, device) -> Decoder:
                    lm_head=None if (lm is None or cfg.tie_embeddings) else lm.to(device).to(torch.bfloat16))
 
 
+# ---- INT8 weights file ------------------------------------------------------------------
+_ATTN = ('q_proj', 'k_proj', 'v_proj', 'o_proj')
+_MLP = ('gate_proj', 'up_proj', 'down_proj')
+
+
+def config_from_hf(d: dict) -> DecoderConfig:
+    """DecoderConfig from a HF Qwen3 config.json dictionary."""
+    heads = d['num_attention_heads']
+    return DecoderConfig(hidden=d['hidden_size'], inter=d['intermediate_size'], layers=d['num_hidden_layers'],
+                         heads=heads, kv_heads=d.get('num_key_value_heads', heads),
+                         head_dim=d.get('head_dim') or d['hidden_size'] // heads, vocab=d['vocab_size'],
+                         eps=d.get('rms_norm_eps', 1e-6), rope_theta=d.get('rope_theta', 1e6),
+                         tie_embeddings=d.get('tie_word_embeddings', True))
+
+
+def config_from_int8(t: dict, ties: dict) -> DecoderConfig:
+    """DecoderConfig inferred from the tensors of an int8-w8a8/1 file (eps and rope theta take
+    the Qwen3 defaults)."""
+    p = 'model.layers.0.'
+    try:
+        vocab, hidden = t['model.embed_tokens.weight'].shape
+        head_dim = t[p + 'self_attn.q_norm.weight'].numel()
+        q_dim = t[p + 'self_attn.q_proj.qweight'].shape[0]
+        kv_dim = t[p + 'self_attn.k_proj.qweight'].shape[0]
+        inter = t[p + 'mlp.gate_proj.qweight'].shape[0]
+    except KeyError as e:
+        raise InvalidModel(f'not a dense Qwen3 decoder: {e.args[0]} missing') from None
+    layers = 1 + max(int(k.split('.')[2]) for k in t if k.startswith('model.layers.'))
+    return DecoderConfig(hidden=hidden, inter=inter, layers=layers, heads=q_dim // head_dim,
+                         kv_heads=kv_dim // head_dim, head_dim=head_dim, vocab=vocab,
+                         tie_embeddings='lm_head.weight' in ties or 'lm_head.weight' not in t)
+
+
+def _expected(cfg: DecoderConfig):
+    """key -> (dtype, shape) of every tensor a dense Qwen3 decoder file holds; the QLinear
+    keys inv_smooth and bias are optional (reported separately)."""
+    bf, H, D = torch.bfloat16, cfg.hidden, cfg.head_dim
+    dims = {'q_proj': (cfg.q_dim, H), 'k_proj': (cfg.kv_dim, H), 'v_proj': (cfg.kv_dim, H),
+            'o_proj': (H, cfg.q_dim), 'gate_proj': (cfg.inter, H), 'up_proj': (cfg.inter, H),
+            'down_proj': (H, cfg.inter)}
+    need = {'model.embed_tokens.weight': (bf, (cfg.vocab, H)), 'model.norm.weight': (bf, (H,)),
+            'lm_head.weight': (bf, (cfg.vocab, H))}
+    opt = {}
+    for i in range(cfg.layers):
+        p = f'model.layers.{i}.'
+        for n in ('input_layernorm', 'post_attention_layernorm'):
+            need[p + n + '.weight'] = (bf, (H,))
+        for n in ('q_norm', 'k_norm'):
+            need[p + 'self_attn.' + n + '.weight'] = (bf, (D,))
+        for grp, names in (('self_attn.', _ATTN), ('mlp.', _MLP)):
+            for n in names:
+                o, k = dims[n]
+                q = p + grp + n
+                need[q + '.qweight'] = (torch.int8, (o, k))
+                need[q + '.wscale'] = (torch.float32, (o,))
+                opt[q + '.inv_smooth'] = (torch.float32, (k,))
+                opt[q + '.bias'] = (torch.float32, (o,))
+    return need, opt
+
+
+def from_int8_state(t: dict, cfg: DecoderConfig, device) -> Decoder:
+    """Builds the decoder from the tensors of an int8-w8a8/1 file: the stored int8 weights,
+    channel scales, smoothing vectors and biases are used as they are (no requantisation).
+    Projections whose input quantisation matches are stacked (q|k|v) or interleaved
+    (gate|up) for the fused kernels; differently smoothed ones stay apart."""
+    need, opt = _expected(cfg)
+    missing = sorted(k for k in need if k not in t and not (k == 'lm_head.weight' and cfg.tie_embeddings))
+    extra = sorted(k for k in t if k not in need and k not in opt)
+    if missing or extra:
+        raise InvalidModel(f'missing {missing[:4]} / unexpected {extra[:4]} (dense Qwen3 decoders only)')
+    for k, v in t.items():
+        dt, shape = need.get(k) or opt[k]
+        if v.dtype != dt or tuple(v.shape) != shape:
+            raise InvalidModel(f'{k}: {v.dtype} {tuple(v.shape)}, expected {dt} {shape}')
+
+    def g(key):
+        v = t.get(key)
+        return None if v is None else v.to(device).contiguous()
+
+    def proj(prefix):
+        return g(prefix + '.qweight'), g(prefix + '.wscale'), g(prefix + '.inv_smooth'), g(prefix + '.bias')
+
+    def cat_bias(ps):
+        if all(b is None for *_, b in ps):
+            return None
+        return torch.cat([b if b is not None else torch.zeros_like(s) for _, s, _, b in ps]).contiguous()
+
+    from .int8_runtime import same_smoothing
+    layers = []
+    for i in range(cfg.layers):
+        p = f'model.layers.{i}.'
+        qkv = [proj(p + 'self_attn.' + n) for n in ('q_proj', 'k_proj', 'v_proj')]
+        bounds = [0, cfg.q_dim, cfg.q_dim + cfg.kv_dim, cfg.q_dim + 2 * cfg.kv_dim]
+        invs = [x[2] for x in qkv]
+        if same_smoothing(invs[0], invs[1]) and same_smoothing(invs[0], invs[2]):
+            parts = None if invs[0] is None else [(0, bounds[3], invs[0])]
+        else:
+            parts = [(bounds[j], bounds[j + 1], invs[j]) for j in range(3)]
+        o_w, o_s, o_inv, o_b = proj(p + 'self_attn.o_proj')
+        gp, up, dp = (proj(p + 'mlp.' + n) for n in _MLP)
+        lay = dict(in_norm=g(p + 'input_layernorm.weight'),
+                   qkv_w=torch.cat([x[0] for x in qkv]).contiguous(), qkv_s=torch.cat([x[1] for x in qkv]).contiguous(),
+                   qkv_b=cat_bias(qkv), qkv_parts=parts,
+                   q_norm=g(p + 'self_attn.q_norm.weight'), k_norm=g(p + 'self_attn.k_norm.weight'),
+                   o_w=o_w, o_s=o_s, o_inv=o_inv, o_b=o_b, post_norm=g(p + 'post_attention_layernorm.weight'),
+                   down_w=dp[0], down_s=dp[1], down_inv=dp[2], down_b=dp[3])
+        if same_smoothing(gp[2], up[2]):
+            bias = None
+            if gp[3] is not None or up[3] is not None:
+                bias = interleave_gate_up(gp[3] if gp[3] is not None else torch.zeros_like(gp[1]),
+                                          up[3] if up[3] is not None else torch.zeros_like(up[1]))
+            lay.update(gu_w=interleave_gate_up(gp[0], up[0]), gu_s=interleave_gate_up(gp[1], up[1]),
+                       gu_inv=gp[2], gu_b=bias)
+        else:
+            lay.update(gu_w=None, gu_s=None, split_mlp=(*gp, *up))
+        layers.append(Layer(**lay))
+    lm = t.get('lm_head.weight')
+    embed = g('model.embed_tokens.weight')
+    tied = lm is None or lm is t['model.embed_tokens.weight']
+    return Decoder(cfg=cfg, embed=embed, layers=layers, final_norm=g('model.norm.weight'),
+                   lm_head=None if tied else lm.to(device).contiguous())
+
+
+def load_model(path, device, cfg: DecoderConfig = None) -> Decoder:
+    """The reference's int8_runtime.load_model (lib/int8_runtime.py:665-726) for dense Qwen3
+    decoders: reads model-int8.safetensors (a folder, with its config.json when present, or
+    the file itself) and builds the Decoder on `device`."""
+    import json
+    from pathlib import Path
+    path = Path(path)
+    tensors, ties = read_int8_file(path)
+    if cfg is None:
+        cj = (path if path.is_dir() else path.parent) / 'config.json'
+        cfg = config_from_hf(json.loads(cj.read_text())) if cj.is_file() else config_from_int8(tensors, ties)
+    return from_int8_state(tensors, cfg, torch.device(device))
+
+
 def random_decoder(cfg: DecoderConfig, device, seed: int = 0, std: float = 0.02) -> Decoder:
     """Random-init decoder of the given dims, generated on the device: bf16 weights N(0, std)
     quantised per output row (as converting a random-init HF model would), norm weights
@@ -165,6 +341,26 @@ def rope_tables(cfg: DecoderConfig, n: int, device):
     return emb.cos().to(torch.bfloat16), emb.sin().to(torch.bfloat16)
 
 
+class _Normed:
+    """A block's normed input, quantised once per distinct smoothing vector: the fused
+    norm kernel's codes serve the first consumer, and the normed activations y (kept only
+    when another consumer smooths differently) are requantised for the others."""
+
+    def __init__(self, q, s, inv, y):
+        self.m = q.shape[0]
+        self.y = y
+        self.cache = {_inv_key(inv): (q, s)}
+
+    def codes(self, inv, rows=None):
+        key = _inv_key(inv)
+        if key not in self.cache:
+            self.cache[key] = torch.ops.mica.act_quant(self.y, inv, K._round_code())
+        q, s = self.cache[key]
+        if rows is None:
+            return q, s
+        return q.index_select(0, rows), s.index_select(0, rows)
+
+
 class Prefill:
     """Scores requests on a Decoder: ids -> option probabilities of the last position."""
 
@@ -188,13 +384,37 @@ class Prefill:
         self.backends = attn_backends
 
     # ---- pieces ------------------------------------------------------------------------
-    def _norm_quant(self, x, w, residual=None):
-        q, s, _, summed = torch.ops.mica.rmsnorm_quant(x, residual, w, None, self.cfg.eps, N.NORM_WEIGHT,
-                                                        K._round_code(), False, True)
-        return q, s, (summed if residual is not None else x)
+    def _norm_quant(self, x, w, residual=None, inv=None, want_y=False):
+        """Fused residual add + RMSNorm + quantisation of y * inv. Returns (q, s, residual
+        stream, y); y (the normed activations) only when want_y."""
+        q, s, y, summed = torch.ops.mica.rmsnorm_quant(x, residual, w, inv, self.cfg.eps, N.NORM_WEIGHT,
+                                                        K._round_code(), want_y, True)
+        return q, s, (summed if residual is not None else x), (y if want_y else None)
 
-    def _gemm(self, q, s, w, sw):
-        return torch.ops.mica.w8a8_gemm(q, s, w, sw, None, 0, K.tiles.tile(w.shape[0], w.shape[1], q.shape[0]))
+    def _normed(self, x, w, residual, inv0, n_inv):
+        q, s, h, y = self._norm_quant(x, w, residual, inv0, want_y=n_inv > 1)
+        return _Normed(q, s, inv0, y), h
+
+    def _gemm(self, q, s, w, sw, bias=None):
+        return torch.ops.mica.w8a8_gemm(q, s, w, sw, bias, 0, K.tiles.tile(w.shape[0], w.shape[1], q.shape[0]))
+
+    def _qkv_cols(self, lay, nq, lo, hi, rows=None):
+        """Columns [lo, hi) of the q|k|v projection of the normed input `nq` (for `rows` only,
+        when given), one GEMM per part that quantises the input differently."""
+        parts = [(max(a, lo), min(b, hi), inv) for a, b, inv in lay.parts() if min(b, hi) > max(a, lo)]
+        bias = lay.qkv_b
+        if len(parts) == 1:
+            a, b, inv = parts[0]
+            q, s = nq.codes(inv, rows)
+            return self._gemm(q, s, lay.qkv_w[a:b], lay.qkv_s[a:b], None if bias is None else bias[a:b])
+        m = nq.m if rows is None else rows.numel()
+        out = torch.empty((m, hi - lo), dtype=torch.bfloat16, device=lay.qkv_w.device)
+        for a, b, inv in parts:
+            q, s = nq.codes(inv, rows)
+            w = lay.qkv_w[a:b]
+            torch.ops.mica.w8a8_gemm_into(q, s, w, lay.qkv_s[a:b], None if bias is None else bias[a:b],
+                                          out[:, a - lo:b - lo], K.tiles.tile(w.shape[0], w.shape[1], m))
+        return out
 
     def _attention(self, q, k, v, causal, mask=None):
         """q [B, Sq, H, D], k/v [B, Sk, KV, D] (strided views are fine) -> [B*Sq, H*D]."""
@@ -205,9 +425,18 @@ class Prefill:
                                                enable_gqa=True)
         return o.transpose(1, 2).reshape(q.shape[0] * q.shape[1], -1).contiguous()
 
-    def _mlp(self, q, s, lay):
-        _, qh, sh = torch.ops.mica.gemm_swiglu_quant(q, s, lay.gu_w, lay.gu_s, None, K._round_code())
-        return self._gemm(qh, sh, lay.down_w, lay.down_s)
+    def _mlp(self, nm, lay):
+        """gate/up + SwiGLU + requant (down_proj's smoothing applied there), then down."""
+        if lay.split_mlp is None:
+            q, s = nm.codes(lay.gu_inv)
+            _, qh, sh = torch.ops.mica.gemm_swiglu_quant(q, s, lay.gu_w, lay.gu_s, lay.gu_b, lay.down_inv,
+                                                         K._round_code())
+        else:
+            g_w, g_s, g_inv, g_b, u_w, u_s, u_inv, u_b = lay.split_mlp
+            g = self._gemm(*nm.codes(g_inv), g_w, g_s, g_b)
+            u = self._gemm(*nm.codes(u_inv), u_w, u_s, u_b)
+            _, qh, sh = torch.ops.mica.swiglu_quant(g, u, lay.down_inv, K._round_code(), False, True)
+        return self._gemm(qh, sh, lay.down_w, lay.down_s, lay.down_b)
 
     def _positions(self, B, L, device):
         """Row positions of a [B, L] batch (None for B = 1: the kernel uses the row index)."""
@@ -234,20 +463,20 @@ class Prefill:
         prev = None
         nl = len(m.layers)
         for li, lay in enumerate(m.layers):
-            q8, s8, h = self._norm_quant(prev if prev is not None else h, lay.in_norm,
-                                         h if prev is not None else None)
+            nq, h = self._normed(prev if prev is not None else h, lay.in_norm, h if prev is not None else None,
+                                 lay.parts()[0][2], lay.distinct_attn_invs())
             if li == nl - 1 and last_only:
-                return self._last_layer(q8, s8, h, lay, B, L, pos, limit)
-            qkv = self._gemm(q8, s8, lay.qkv_w, lay.qkv_s)
+                return self._last_layer(nq, h, lay, B, L, pos, limit)
+            qkv = self._qkv_cols(lay, nq, 0, lay.qkv_w.shape[0])
             torch.ops.mica.qk_norm_rope(qkv, lay.q_norm, lay.k_norm, self.cos, self.sin, pos, 0, cfg.heads,
                                         cfg.kv_heads, cfg.eps)
             q, k, v = qkv.split([cfg.q_dim, cfg.kv_dim, cfg.kv_dim], dim=1)
             attn = self._attention(q.view(B, L, cfg.heads, cfg.head_dim), k.view(B, L, cfg.kv_heads, cfg.head_dim),
                                    v.view(B, L, cfg.kv_heads, cfg.head_dim), causal=True)
-            qa, sa = torch.ops.mica.act_quant(attn, None, K._round_code())
-            o = self._gemm(qa, sa, lay.o_w, lay.o_s)
-            q8, s8, h = self._norm_quant(o, lay.post_norm, h)
-            prev = self._mlp(q8, s8, lay)
+            qa, sa = torch.ops.mica.act_quant(attn, lay.o_inv, K._round_code())
+            o = self._gemm(qa, sa, lay.o_w, lay.o_s, lay.o_b)
+            nm, h = self._normed(o, lay.post_norm, h, lay.mlp_in_inv(), lay.distinct_mlp_invs())
+            prev = self._mlp(nm, lay)
         out = h + prev
         return out.index_select(0, self._scored_rows(B, L, limit, out.device))
 
@@ -255,30 +484,30 @@ class Prefill:
         base = torch.arange(B, device=device, dtype=torch.long) * L
         return base + ((limit.view(B) - 1) if limit is not None else L - 1)
 
-    def _last_layer(self, q8, s8, h, lay, B, L, pos, limit):
+    def _last_layer(self, nq, h, lay, B, L, pos, limit):
         """K/V for every row, Q / attention / O / MLP for each request's scored row only."""
         cfg = self.cfg
         qd, kd = cfg.q_dim, cfg.kv_dim
-        dev = q8.device
-        kv = self._gemm(q8, s8, lay.qkv_w[qd:], lay.qkv_s[qd:])
+        dev = h.device
+        kv = self._qkv_cols(lay, nq, qd, qd + 2 * kd)
         torch.ops.mica.qk_norm_rope(kv, None, lay.k_norm, self.cos, self.sin, pos, 0, 0, cfg.kv_heads, cfg.eps)
         k, v = kv.split([kd, kd], dim=1)
         rows = self._scored_rows(B, L, limit, dev)
-        row_q8, row_s8, res = q8.index_select(0, rows), s8.index_select(0, rows), h.index_select(0, rows)
+        res = h.index_select(0, rows)
         qpos = (limit.view(B) - 1) if limit is not None else torch.full((B,), L - 1, dtype=torch.long, device=dev)
         mask = None
         if limit is not None:
             keys = torch.arange(L, device=dev)
             mask = torch.where(keys[None, :] < limit.view(B, 1), 0.0, float('-inf')).to(torch.bfloat16)
             mask = mask.view(B, 1, 1, L)
-        q = self._gemm(row_q8, row_s8, lay.qkv_w[:qd], lay.qkv_s[:qd])
+        q = self._qkv_cols(lay, nq, 0, qd, rows)
         torch.ops.mica.qk_norm_rope(q, lay.q_norm, None, self.cos, self.sin, qpos, 0, cfg.heads, 0, cfg.eps)
         attn = self._attention(q.view(B, 1, cfg.heads, cfg.head_dim), k.view(B, L, cfg.kv_heads, cfg.head_dim),
                                v.view(B, L, cfg.kv_heads, cfg.head_dim), causal=False, mask=mask)
-        qa, sa = torch.ops.mica.act_quant(attn, None, K._round_code())
-        o = self._gemm(qa, sa, lay.o_w, lay.o_s)
-        q8r, s8r, res = self._norm_quant(o, lay.post_norm, res)
-        d = self._mlp(q8r, s8r, lay)
+        qa, sa = torch.ops.mica.act_quant(attn, lay.o_inv, K._round_code())
+        o = self._gemm(qa, sa, lay.o_w, lay.o_s, lay.o_b)
+        nm, res = self._normed(o, lay.post_norm, res, lay.mlp_in_inv(), lay.distinct_mlp_invs())
+        d = self._mlp(nm, lay)
         return res + d
 
     def probs(self, h_last: torch.Tensor, lo=None, hi=None):

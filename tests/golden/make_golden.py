@@ -3,7 +3,7 @@
 Run in the build container, where the reference checkout is available (it is read, never
 copied; only inputs/outputs are saved):
 
-    python tests/golden/make_golden.py [/path/to/reference]
+    python tests/golden/make_golden.py [/path/to/reference] [set names, e.g. model_int8]
 
 What runs (all on CPU):
   * the reference's Triton kernels v0.5/serving/kernel_src/kernels.py act_quant and mm_i8,
@@ -236,6 +236,72 @@ def model_cases(g):
     return {'m': out}
 
 
+@torch.no_grad()
+def model_int8_cases(g):
+    """An int8-w8a8/1 weights folder (model_int8/: model-int8.safetensors + config.json) of a
+    tiny dense Qwen3 converted by the reference's int8_runtime.convert WITH activation
+    statistics, so its QLinears carry inv_smooth (lib/int8_runtime.py:195-206):
+      layer 0: no statistics (no smoothing: the fused q|k|v and gate|up paths);
+      layer 1: statistics for every projection (per-projection smoothing: q, k, v and gate,
+               up each quantise their shared input differently);
+      layer 2: statistics for o_proj and down_proj only (the fused MLP with down smoothing).
+    The file holds the converted model's state dict (the reference QLinear buffer names), with
+    lm_head tied to the embedding through the `ties` metadata; golden option probabilities come
+    from the converted model itself (QLinear 'emulate')."""
+    import json
+    from safetensors.torch import save_file
+    from transformers import Qwen3Config, Qwen3ForCausalLM
+    cfg = Qwen3Config(**MODEL_DIMS)
+    cfg._attn_implementation = 'eager'
+    torch.manual_seed(20261203)
+    model = Qwen3ForCausalLM(cfg).eval()
+    for name, prm in model.named_parameters():
+        if name.endswith('norm.weight'):
+            prm.data = 1 + 0.1 * torch.randn(prm.shape, generator=g)
+    model = model.to(torch.bfloat16)
+
+    def amax(k):
+        a = torch.exp(torch.randn(k, generator=g))
+        a[torch.randperm(k, generator=g)[:4]] *= 20.0          # outlier channels
+        return a
+
+    H, Q, I = cfg.hidden_size, cfg.num_attention_heads * cfg.head_dim, cfg.intermediate_size
+    stats = {}
+    x_attn, x_mlp = amax(H), amax(H)
+    for n in ('q_proj', 'k_proj', 'v_proj'):
+        stats[f'layers.1.self_attn.{n}'] = x_attn                 # one input, per-projection factors
+    for n in ('gate_proj', 'up_proj'):
+        stats[f'layers.1.mlp.{n}'] = x_mlp
+    for i in (1, 2):
+        stats[f'layers.{i}.self_attn.o_proj'] = amax(Q)
+        stats[f'layers.{i}.mlp.down_proj'] = amax(I)
+    replaced, smoothed = rt.convert(model.model, stats, 'emulate')
+    assert replaced == 7 * cfg.num_hidden_layers and smoothed == 9, (replaced, smoothed)
+    state = model.state_dict()
+    ties = {'lm_head.weight': 'model.embed_tokens.weight'}
+    stored = {k: v.contiguous() for k, v in state.items() if k not in ties}
+    folder = HERE / 'model_int8'
+    folder.mkdir(exist_ok=True)
+    save_file(stored, str(folder / rt.FILE), metadata={'format': rt.FILE_FORMAT, 'ties': json.dumps(ties)})
+    (folder / 'config.json').write_text(json.dumps({**MODEL_DIMS, 'architectures': ['Qwen3ForCausalLM'],
+                                                    'model_type': 'qwen3'}, indent=1, sort_keys=True) + '\n')
+    options = torch.randperm(cfg.vocab_size, generator=g)[:40]
+    weight = model.get_output_embeddings().weight.detach().index_select(0, options).float().clone()
+    out = {'options': options.numpy().astype(np.int64)}
+    for i, n in enumerate((45, 130)):
+        ids = torch.randint(0, cfg.vocab_size, (n,), generator=g)
+        hid = model.model(ids[None]).last_hidden_state[:, -1]
+        z = torch.nn.functional.linear(hid.float(), weight).float()
+        lo, hi = (2, 2 + 23) if i == 0 else (0, 40)
+        p = torch.zeros_like(z)
+        p[:, lo:hi] = z[:, lo:hi].softmax(-1)
+        out[f'ids{i}'] = ids.numpy().astype(np.int64)
+        out[f'logits{i}'] = z.numpy()
+        out[f'probs{i}'] = p.numpy()
+        out[f'slice{i}'] = np.array([lo, hi], np.int32)
+    return {'m': out}
+
+
 def save(name, cases):
     flat = {f'{c}/{k}': v for c, d in cases.items() for k, v in d.items()}
     np.savez_compressed(HERE / f'{name}.npz', **flat)
@@ -243,10 +309,13 @@ def save(name, cases):
 
 
 if __name__ == '__main__':
+    # optional names after the reference path regenerate only those sets
+    only = set(sys.argv[2:])
     g = torch.Generator().manual_seed(20261201)
-    save('act_quant', act_cases(g))
-    save('gemm', gemm_cases(g))
-    save('norm', norm_cases(g))
-    save('readout', readout_cases(g))
-    save('selftest', selftest_cases(g))
-    save('model', model_cases(g))
+    for name, fn in (('act_quant', act_cases), ('gemm', gemm_cases), ('norm', norm_cases),
+                     ('readout', readout_cases), ('selftest', selftest_cases), ('model', model_cases)):
+        cases = fn(g)                     # every set draws from the one generator, in this order
+        if not only or name in only:
+            save(name, cases)
+    if not only or 'model_int8' in only:
+        save('model_int8', model_int8_cases(torch.Generator().manual_seed(20261203)))

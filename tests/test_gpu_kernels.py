@@ -305,3 +305,69 @@ def test_act_quant_exact_ties_and_boundaries(K):
             K.ROUND['mode'] = 'half_away'
         qo, so = O.quant_act(x.float().numpy(), None, mode)
         assert np.array_equal(q.cpu().numpy(), qo) and np.array_equal(s.cpu().numpy(), so)
+
+
+# ---------------------------------------------------------------------------------------
+# SwiGLU + requantisation for MLPs whose gate and up projections are smoothed differently
+# (mica_swiglu_quant), and down_proj's smoothing inside the fused gate_up kernel.
+@pytest.mark.parametrize('mode', ['half_away', 'half_even'])
+@pytest.mark.parametrize('smooth', [False, True])
+@pytest.mark.parametrize('m,i', [(1, 64), (37, 256), (608, 9728)])
+def test_swiglu_quant_vs_oracle(K, m, i, smooth, mode):
+    g = torch.Generator().manual_seed(m + i + smooth)
+    gate = (torch.randn(m, i, generator=g) * 3).to(torch.bfloat16)
+    up = (torch.randn(m, i, generator=g) * 2).to(torch.bfloat16)
+    inv = torch.exp(torch.randn(i, generator=g)) if smooth else None
+    K.ROUND['mode'] = mode
+    try:
+        h, q, s = K.swiglu_quant(gate.cuda(), up.cuda(), None if inv is None else inv.cuda(), want_h=True)
+        h_only = K.swi_glu(gate.cuda(), up.cuda())
+    finally:
+        K.ROUND['mode'] = 'half_away'
+    h_ref = O.silu_mul(gate.float().numpy(), up.float().numpy())
+    hk = to_np(h)
+    assert np.allclose(hk, h_ref, rtol=1e-2, atol=1e-2 * np.abs(h_ref).max())
+    assert (hk != h_ref).mean() < 0.01
+    assert torch.equal(h_only, h)
+    q2, s2 = O.quant_act(hk, None if inv is None else inv.numpy(), mode)
+    assert np.array_equal(s.cpu().numpy(), s2)
+    assert np.array_equal(q.cpu().numpy(), q2)
+
+
+@pytest.mark.parametrize('m,i,k', [(37, 256, 2560), (1024, 9728, 2560)])
+def test_gemm_swiglu_quant_down_smoothing(K, m, i, k):
+    """inv_h (down_proj's inv_smooth): the fused requantisation quantises h * inv_h."""
+    g = torch.Generator().manual_seed(m * 3 + i)
+    qx = torch.randint(-127, 128, (m, k), generator=g, dtype=torch.int8)
+    sx = torch.rand(m, generator=g) * 0.02 + 1e-3
+    wg = torch.randint(-127, 128, (i, k), generator=g, dtype=torch.int8)
+    wu = torch.randint(-127, 128, (i, k), generator=g, dtype=torch.int8)
+    sg = torch.rand(i, generator=g) * 9e-3 + 1e-3
+    su = torch.rand(i, generator=g) * 9e-3 + 1e-3
+    inv = torch.exp(torch.randn(i, generator=g))
+    qw = torch.from_numpy(O.interleave_gate_up(wg.numpy(), wu.numpy())).contiguous()
+    sw = torch.from_numpy(O.interleave_gate_up(sg.numpy(), su.numpy())).contiguous()
+    h, q, s = K.mm_i8_swiglu_quant(qx.cuda(), sx.cuda(), qw.cuda(), sw.cuda(), None, inv.cuda())
+    h_ref, _, _ = O.gate_up_swiglu_quant(qx.numpy(), sx.numpy(), wg.numpy(), sg.numpy(), wu.numpy(), su.numpy())
+    hk = to_np(h)
+    assert np.allclose(hk, h_ref, rtol=1e-2, atol=1e-2 * np.abs(h_ref).max())
+    q2, s2 = O.quant_act_half_away(hk, inv.numpy())
+    assert np.array_equal(s.cpu().numpy(), s2)
+    assert np.array_equal(q.cpu().numpy(), q2)
+    assert dev_error() == 0
+
+
+def test_gemm_into_column_slices_bit_exact(K):
+    """w8a8_gemm_into writes each projection into its column slice of one q|k|v buffer."""
+    m, k = 300, 512
+    g = torch.Generator().manual_seed(5)
+    qx = torch.randint(-127, 128, (m, k), generator=g, dtype=torch.int8).cuda()
+    sx = (torch.rand(m, generator=g) * 0.05 + 1e-3).cuda()
+    out = torch.full((m, 384), 7.0, dtype=torch.bfloat16, device='cuda')
+    refs = []
+    for lo, hi in ((0, 256), (256, 320), (320, 384)):
+        w = torch.randint(-127, 128, (hi - lo, k), generator=g, dtype=torch.int8).cuda()
+        sw = (torch.rand(hi - lo, generator=g) * 9e-3 + 1e-3).cuda()
+        torch.ops.mica.w8a8_gemm_into(qx, sx, w, sw, None, out[:, lo:hi], 0)
+        refs.append(torch.ops.mica.w8a8_gemm(qx, sx, w, sw, None, 0, 0))
+    assert torch.equal(out, torch.cat(refs, dim=1))

@@ -162,3 +162,40 @@ def test_batched_scoring_matches_single_requests():
         z1, p1 = pf.score(t, *slices[i], graphs=False)
         assert torch.allclose(pb[i:i + 1], p1, atol=2e-3, rtol=0), i
         assert abs(float(pb[i].sum()) - 1.0) < 1e-4
+
+
+# ---------------------------------------------------------------------------------------
+# A model read from an int8-w8a8/1 weights folder written by the reference's convert with
+# activation statistics: per-projection smoothing (split q/k/v and gate/up paths), down and
+# o smoothing, tied lm_head. Probabilities against the converted reference model's own.
+@pytest.fixture(scope='module')
+def int8_file_model():
+    from conftest import GOLDEN
+    from mica_b200 import prefill as P
+    g = golden('model_int8')
+    model = P.load_model(GOLDEN / 'model_int8', 'cuda')
+    return P.Prefill(model, torch.from_numpy(g['m/options']), max_len=512), g
+
+
+@pytest.mark.parametrize('i', [0, 1])
+def test_int8_file_model_probs_match_reference(int8_file_model, i):
+    import mica_b200.int8_kernels as K
+    pf, g = int8_file_model
+    ids = torch.from_numpy(g[f'm/ids{i}']).cuda()
+    lo, hi = (int(v) for v in g[f'm/slice{i}'])
+    K.ROUND['mode'] = 'half_even'      # the reference's QLinear 'emulate' path rounds half to even
+    try:
+        z, p = pf.score(ids, lo, hi, graphs=False)
+        pf.capture(pf.bucket(int(ids.shape[0])))
+        zg, pg = (t.clone() for t in pf.score(ids, lo, hi, graphs=True))
+        pf.release()
+        z_full, p_full = pf.probs(pf.hidden_last(ids, last_only=False), torch.tensor([lo], dtype=torch.int32,
+                                                                                      device='cuda'),
+                                  torch.tensor([hi], dtype=torch.int32, device='cuda'))
+    finally:
+        K.ROUND['mode'] = 'half_away'
+    ref_p, ref_z = g[f'm/probs{i}'], g[f'm/logits{i}']
+    assert np.abs(p.cpu().numpy() - ref_p).max() < 1e-3
+    assert np.abs(z.cpu().numpy() - ref_z).max() < 2e-2 * max(1.0, float(np.abs(ref_z).max()))
+    assert torch.allclose(pg, p, atol=1e-3, rtol=0)                     # graph replay vs eager
+    assert np.abs(p_full.cpu().numpy() - p.cpu().numpy()).max() < 1e-3   # last-row restriction

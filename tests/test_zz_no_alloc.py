@@ -51,7 +51,7 @@ def _call_workspace(N, qx, sx, qw, sw, m, i, k):
     h, q, s = _outputs(m, i)
     ws = torch.empty(N.lib().mica_swiglu_workspace_bytes(m), dtype=torch.uint8, device='cuda')
     N.call('mica_w8a8_gemm_swiglu_quant', qx.data_ptr(), k, qw.data_ptr(), k, sx.data_ptr(), sw.data_ptr(), None,
-           h.data_ptr(), i, q.data_ptr(), i, s.data_ptr(), m, i, k, 0, ws.data_ptr(), ws.numel(),
+           None, h.data_ptr(), i, q.data_ptr(), i, s.data_ptr(), m, i, k, 0, ws.data_ptr(), ws.numel(),
            torch.cuda.current_stream().cuda_stream)
     return h, q, s
 
@@ -59,7 +59,7 @@ def _call_workspace(N, qx, sx, qw, sw, m, i, k):
 def _call_noalloc(N, qx, sx, qw, sw, m, i, k):
     h, q, s = _outputs(m, i)
     N.call('mica_w8a8_gemm_swiglu_quant_noalloc', qx.data_ptr(), k, qw.data_ptr(), k, sx.data_ptr(), sw.data_ptr(),
-           None, h.data_ptr(), i, q.data_ptr(), i, s.data_ptr(), m, i, k, 0, torch.cuda.current_stream().cuda_stream)
+           None, None, h.data_ptr(), i, q.data_ptr(), i, s.data_ptr(), m, i, k, 0, torch.cuda.current_stream().cuda_stream)
     return h, q, s
 
 
@@ -92,7 +92,8 @@ def test_noalloc_rejects_rows_beyond_its_fixed_scratch(lib):
     m, i, k = 65537, 128, 64     # one row over MICA_NOALLOC_MAX_ROWS; refused before any launch
     dummy = torch.empty(16, dtype=torch.int8, device='cuda')
     rc = lib.lib().mica_w8a8_gemm_swiglu_quant_noalloc(dummy.data_ptr(), k, dummy.data_ptr(), k, dummy.data_ptr(),
-                                                        dummy.data_ptr(), None, dummy.data_ptr(), i, dummy.data_ptr(),
+                                                        dummy.data_ptr(), None, None, dummy.data_ptr(), i,
+                                                        dummy.data_ptr(),
                                                         i, dummy.data_ptr(), m, i, k, 0,
                                                         torch.cuda.current_stream().cuda_stream)
     assert rc == 7   # MICA_ERR_WORKSPACE
