@@ -85,7 +85,7 @@ typedef struct mica_caps {
     int pair_clusters;      /* co-resident CTA pairs for the 256-row GEMM tiles         */
 } mica_caps;
 
-#define MICA_ABI_VERSION 2
+#define MICA_ABI_VERSION 3
 
 /* Capability query. Replaces int8_kernels.available() (v0.5/serving/lib/int8_kernels.py:146-159)
  * and the capability probe in _device_cc (:130-143). Fills *caps for `device`.         */
@@ -148,11 +148,16 @@ int mica_w8a8_gemm(const int8_t* A, long lda, const int8_t* B, long ldb,
  *   block_m 128 = one CTA per tile; 256 = a pair of CTAs on two SMs sharing each MMA
  *           (tcgen05 cta_group::2), 0 = library choice;
  *   block_n 64 / 128 / 256 (pairs: 128 / 256), 0 = library choice;
- *   max_ctas caps the persistent grid (0 = all SMs / all co-resident pairs).             */
+ *   max_ctas caps the persistent grid (0 = all SMs / all co-resident pairs);
+ *   splits   K split of each 128-row tile across a cluster of that many CTAs, reduced in
+ *           distributed shared memory (exact): 0 = library choice (split only when fewer
+ *           than half the SMs would get a tile), 1 = never, 2..8 = forced (MICA_ERR_UNSUPPORTED
+ *           when a rank would get no k-block). Ignored with max_ctas > 0; not with block_m 256. */
 int mica_w8a8_gemm_cfg(const int8_t* A, long lda, const int8_t* B, long ldb,
                        const float* sa, const float* sb, const float* bias,
                        void* C, int c_dtype, long ldc,
-                       int M, int N, int K, int block_m, int block_n, int max_ctas, void* stream);
+                       int M, int N, int K, int block_m, int block_n, int max_ctas, int splits,
+                       void* stream);
 
 /* Fused MLP front half: gate_up W8A8 GEMM + SwiGLU + next-layer per-token quantisation.
  *   Bgu [2*I, K]: gate and up weight rows interleaved in groups of 16

@@ -69,7 +69,7 @@ SIGNATURES = {
         [_P, _I, _L, _P, _L, _P, _I, _F, _P, _P, _L, _P, _L, _P, _L, _P, _I, _I, _I, _P],
     ),
     'mica_w8a8_gemm': (_I, [_P, _L, _P, _L, _P, _P, _P, _P, _I, _L, _I, _I, _I, _P]),
-    'mica_w8a8_gemm_cfg': (_I, [_P, _L, _P, _L, _P, _P, _P, _P, _I, _L, _I, _I, _I, _I, _I, _I, _P]),
+    'mica_w8a8_gemm_cfg': (_I, [_P, _L, _P, _L, _P, _P, _P, _P, _I, _L, _I, _I, _I, _I, _I, _I, _I, _P]),
     'mica_swiglu_workspace_bytes': (_Z, [_I]),
     'mica_w8a8_gemm_swiglu_quant': (
         _I,

@@ -16,6 +16,7 @@
 #include "common.cuh"
 #include "gemm_i8.cuh"
 #include "gemm_i8_pair.cuh"
+#include "gemm_i8_splitk.cuh"
 #include "quant.cuh"
 #include "readout.cuh"
 #include "qk_rope.cuh"
@@ -218,6 +219,92 @@ static int pair_launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUten
 // Tile choice when the caller (or the pinned table in the Python layer) gives none,
 // from the measured sweep over the 4B model's projection shapes: the single-CTA 128 x 256
 // tile wins whenever it fills a wave of SMs; below that 128 x 128, then 128 x 64.
+// ---- split-K clusters ----------------------------------------------------------------
+// Co-resident clusters of S split-K CTAs, per device, per tile width and S (0 = not queried).
+static std::atomic<int> g_splitk_clusters[kMaxDev][3][9];
+
+static int bn_index(int bn) { return bn == 256 ? 2 : (bn == 128 ? 1 : 0); }
+
+template <int BN, typename OutT>
+static int splitk_prepare(int dev) {
+    static std::atomic<uint64_t> done{0};
+    const uint64_t bit = 1ull << (dev & 63);
+    if (done.load(std::memory_order_acquire) & bit) return MICA_OK;
+    cudaError_t e = cudaFuncSetAttribute(gemm_i8_splitk_kernel<BN, OutT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         GemmShape<BN, 4>::SMEM_BYTES);
+    if (e != cudaSuccess) { set_cuda_error(e); return MICA_ERR_CUDA; }
+    for (int s = 2; s <= 8; ++s) {
+        if (g_splitk_clusters[dev][bn_index(BN)][s].load() != 0) continue;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(s * 64);
+        cfg.blockDim = dim3(GemmShape<BN, 4>::THREADS);
+        cfg.dynamicSmemBytes = GemmShape<BN, 4>::SMEM_BYTES;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = s;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        int n = 0;
+        e = cudaOccupancyMaxActiveClusters(&n, gemm_i8_splitk_kernel<BN, OutT>, &cfg);
+        if (e != cudaSuccess) { set_cuda_error(e); return MICA_ERR_CUDA; }
+        g_splitk_clusters[dev][bn_index(BN)][s].store(n > 0 ? n : -1);
+    }
+    done.fetch_or(bit, std::memory_order_release);
+    return MICA_OK;
+}
+
+// The split factor for `tiles` output tiles of `num_kb` k-blocks: 1 (no split) unless fewer
+// than half the SMs would get a tile; then the largest S <= 8 whose clusters are all
+// co-resident, that keeps at least four k-blocks per rank, and leaves no rank empty.
+static int choose_splits(int dev, int bn, long tiles, int num_kb, int sms) {
+    if (2 * tiles > sms) return 1;
+    for (int s = 8; s >= 2; --s) {
+        const int co = g_splitk_clusters[dev][bn_index(bn)][s].load();
+        const int per = (num_kb + s - 1) / s;
+        if (co > 0 && tiles <= co && per >= 4 && (s - 1) * per < num_kb) return s;
+    }
+    return 1;
+}
+
+template <int BN, typename OutT>
+static int splitk_launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const GemmArgs& args,
+                         long tiles, int splits, cudaStream_t stream) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(tiles * splits));
+    cfg.blockDim = dim3(GemmShape<BN, 4>::THREADS);
+    cfg.dynamicSmemBytes = GemmShape<BN, 4>::SMEM_BYTES;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = splits;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_i8_splitk_kernel<BN, OutT>, ta, tb, tc, args);
+    if (e != cudaSuccess) { set_cuda_error(e); return MICA_ERR_CUDA; }
+    return launch_status();
+}
+
+template <int BN>
+static int splitk_prepare_all(int dev) {
+    int rc;
+    if ((rc = splitk_prepare<BN, __nv_bfloat16>(dev)) || (rc = splitk_prepare<BN, __half>(dev)) ||
+        (rc = splitk_prepare<BN, float>(dev)))
+        return rc;
+    return MICA_OK;
+}
+
+template <int BN>
+static int splitk_dispatch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const GemmArgs& g,
+                           int c_dtype, long tiles, int splits, cudaStream_t st) {
+    if (c_dtype == MICA_DT_BF16) return splitk_launch<BN, __nv_bfloat16>(ta, tb, tc, g, tiles, splits, st);
+    if (c_dtype == MICA_DT_FP16) return splitk_launch<BN, __half>(ta, tb, tc, g, tiles, splits, st);
+    return splitk_launch<BN, float>(ta, tb, tc, g, tiles, splits, st);
+}
+
 static void pick_tile(int M, int N, int sms, int* bm, int* bn) {
     const long m_blocks = (M + 127) / 128;
     const long t256 = m_blocks * ((N + 255) / 256);
@@ -298,6 +385,12 @@ int mica_preload(int* n_kernels) {
     PREP_PAIR(128, float)
     PREP_PAIR(256, float)
 #undef PREP_PAIR
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if ((rc = splitk_prepare_all<64>(dev)) || (rc = splitk_prepare_all<128>(dev)) ||
+        (rc = splitk_prepare_all<256>(dev)))
+        return rc;
+    n += 9;
     if (n_kernels) *n_kernels = n;
     return MICA_OK;
 }
@@ -409,13 +502,13 @@ static int gemm_dispatch_out(const CUtensorMap& ta, const CUtensorMap& tb, const
 
 int mica_w8a8_gemm_cfg(const int8_t* A, long lda, const int8_t* B, long ldb, const float* sa, const float* sb,
                        const float* bias, void* C, int c_dtype, long ldc, int M, int N, int K, int block_m,
-                       int block_n, int max_ctas, void* stream) {
+                       int block_n, int max_ctas, int splits, void* stream) {
     int rc = gemm_checks(A, lda, B, ldb, sa, sb, bias, C, c_dtype, ldc, M, N, K);
     if (rc) return rc;
     if (block_m != 0 && block_m != 128 && block_m != 256) return MICA_ERR_ARG;
     if (block_n != 0 && block_n != 64 && block_n != 128 && block_n != 256) return MICA_ERR_ARG;
     if (block_m == 256 && block_n == 64) return MICA_ERR_ARG;
-    if (max_ctas < 0) return MICA_ERR_ARG;
+    if (max_ctas < 0 || splits < 0 || splits > 8 || (splits > 1 && block_m == 256)) return MICA_ERR_ARG;
     int sms = 0;
     if ((rc = check_device(&sms))) return rc;
     if (M == 0) return MICA_OK;
@@ -455,6 +548,27 @@ int mica_w8a8_gemm_cfg(const int8_t* A, long lda, const int8_t* B, long ldb, con
         return pair_launch<128, float>(ta, tb, tc, g, tiles, max_ctas, st);
     }
     const long tiles = static_cast<long>((M + 127) / 128) * ((N + bn - 1) / bn);
+    if (splits != 1 && max_ctas == 0) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if ((rc = bn == 256 ? splitk_prepare_all<256>(dev) : bn == 128 ? splitk_prepare_all<128>(dev)
+                                                                        : splitk_prepare_all<64>(dev)))
+            return rc;
+        const int num_kb = (K + 127) / 128;
+        int s = splits;
+        if (s == 0) {
+            s = choose_splits(dev, bn, tiles, num_kb, sms);
+        } else {
+            const int per = (num_kb + s - 1) / s;
+            const int co = g_splitk_clusters[dev][bn_index(bn)][s].load();
+            if ((s - 1) * per >= num_kb || co <= 0) return MICA_ERR_UNSUPPORTED;   // a rank would be empty
+        }
+        if (s > 1) {
+            if (bn == 256) return splitk_dispatch<256>(ta, tb, tc, g, c_dtype, tiles, s, st);
+            if (bn == 128) return splitk_dispatch<128>(ta, tb, tc, g, c_dtype, tiles, s, st);
+            return splitk_dispatch<64>(ta, tb, tc, g, c_dtype, tiles, s, st);
+        }
+    }
     int grid = static_cast<int>(tiles < sms ? tiles : sms);
     if (max_ctas > 0 && grid > max_ctas) grid = max_ctas;
     if (bn == 256) return gemm_dispatch_out<256>(ta, tb, tc, g, c_dtype, grid, st);
@@ -464,7 +578,7 @@ int mica_w8a8_gemm_cfg(const int8_t* A, long lda, const int8_t* B, long ldb, con
 
 int mica_w8a8_gemm(const int8_t* A, long lda, const int8_t* B, long ldb, const float* sa, const float* sb,
                    const float* bias, void* C, int c_dtype, long ldc, int M, int N, int K, void* stream) {
-    return mica_w8a8_gemm_cfg(A, lda, B, ldb, sa, sb, bias, C, c_dtype, ldc, M, N, K, 0, 0, 0, stream);
+    return mica_w8a8_gemm_cfg(A, lda, B, ldb, sa, sb, bias, C, c_dtype, ldc, M, N, K, 0, 0, 0, 0, stream);
 }
 
 // ---------------------------------------------------------------------------------------

@@ -105,15 +105,21 @@ def _(x, residual, gamma, inv, eps, style, round_mode, want_y, want_q):
 @torch.library.custom_op('mica::w8a8_gemm', mutates_args=())
 def w8a8_gemm(qx: torch.Tensor, sx: torch.Tensor, qw: torch.Tensor, sw: torch.Tensor, bias: Optional[torch.Tensor],
               out_dtype: int, tile: int) -> torch.Tensor:
-    """tile = block_m * 1000 + block_n (e.g. 256256 = CTA pair, 256 x 256), 0 = library choice."""
+    """tile = splits * 10**6 + block_m * 1000 + block_n (e.g. 256256 = CTA pair, 256 x 256;
+    1128064 = 128 x 64 never split; 4128256 = 128 x 256 split four ways), 0 = library choice."""
     m, k = qx.shape
     n = qw.shape[0]
     out = torch.empty((m, n), dtype=OUT_DTYPES[out_dtype], device=qx.device)
     with _on(qx):
         N.call('mica_w8a8_gemm_cfg', qx.data_ptr(), qx.stride(0), qw.data_ptr(), qw.stride(0), sx.data_ptr(),
-               sw.data_ptr(), _ptr(bias), out.data_ptr(), out_dtype, out.stride(0), m, n, k, tile // 1000, tile % 1000,
-               0, _stream(qx))
+               sw.data_ptr(), _ptr(bias), out.data_ptr(), out_dtype, out.stride(0), m, n, k, *_tile_args(tile),
+               _stream(qx))
     return out
+
+
+def _tile_args(tile: int):
+    """(block_m, block_n, max_ctas, splits) of a tile code."""
+    return (tile // 1000) % 1000, tile % 1000, 0, tile // 1000000
 
 
 @w8a8_gemm.register_fake
@@ -134,8 +140,8 @@ def w8a8_gemm_into(qx: torch.Tensor, sx: torch.Tensor, qw: torch.Tensor, sw: tor
     n = qw.shape[0]
     with _on(qx):
         N.call('mica_w8a8_gemm_cfg', qx.data_ptr(), qx.stride(0), qw.data_ptr(), qw.stride(0), sx.data_ptr(),
-               sw.data_ptr(), _ptr(bias), out.data_ptr(), _OUT_CODE[out.dtype], out.stride(0), m, n, k, tile // 1000,
-               tile % 1000, 0, _stream(qx))
+               sw.data_ptr(), _ptr(bias), out.data_ptr(), _OUT_CODE[out.dtype], out.stride(0), m, n, k,
+               *_tile_args(tile), _stream(qx))
 
 
 @w8a8_gemm_into.register_fake

@@ -23,7 +23,10 @@ HERE = Path(__file__).resolve().parent
 PINNED = HERE / 'tiles_sm100a.json'
 STATE_NAME = 'tiles_sm100a.json'
 CLASSES = ((128, 's'), (384, 'm'), (1024, 'n'))
-CHOICES = (128064, 128128, 128256, 256128, 256256)
+# tile = splits * 10**6 + block_m * 1000 + block_n: 128-row tiles split K across a cluster when
+# few tiles would leave SMs idle (the library's choice), or never (the 1xxxxxx codes); 256-row
+# tiles run on CTA pairs.
+CHOICES = (128064, 128128, 128256, 256128, 256256, 1128064, 1128128, 1128256)
 
 _TABLE = None
 _LOCK = threading.Lock()

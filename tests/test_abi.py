@@ -57,9 +57,11 @@ def test_entry_points_reject_bad_arguments_without_touching_a_gpu(lib_path):
     assert lib.mica_act_quant(17, 0, 64, None, 16, 64, 16, 4, 64, 0, None) == 3                # misaligned
     assert lib.mica_w8a8_gemm(16, 24, 16, 24, 16, 16, None, 16, 0, 8, 4, 8, 24, None) == 2     # K % 16
     assert lib.mica_w8a8_gemm(16, 32, 16, 32, 16, 16, None, 16, 0, 4, 4, 4, 32, None) == 3     # ldc*2 % 16
-    assert lib.mica_w8a8_gemm_cfg(16, 32, 16, 32, 16, 16, None, 16, 0, 8, 4, 8, 32, 0, 96, 0, None) == 1  # block_n
-    assert lib.mica_w8a8_gemm_cfg(16, 32, 16, 32, 16, 16, None, 16, 0, 8, 4, 8, 32, 192, 0, 0, None) == 1  # block_m
-    assert lib.mica_w8a8_gemm_cfg(16, 32, 16, 32, 16, 16, None, 16, 0, 8, 4, 8, 32, 256, 64, 0, None) == 1
+    assert lib.mica_w8a8_gemm_cfg(16, 32, 16, 32, 16, 16, None, 16, 0, 8, 4, 8, 32, 0, 96, 0, 0, None) == 1  # block_n
+    assert lib.mica_w8a8_gemm_cfg(16, 32, 16, 32, 16, 16, None, 16, 0, 8, 4, 8, 32, 192, 0, 0, 0, None) == 1  # block_m
+    assert lib.mica_w8a8_gemm_cfg(16, 32, 16, 32, 16, 16, None, 16, 0, 8, 4, 8, 32, 256, 64, 0, 0, None) == 1
+    assert lib.mica_w8a8_gemm_cfg(16, 32, 16, 32, 16, 16, None, 16, 0, 8, 4, 8, 32, 128, 64, 0, 9, None) == 1  # splits
+    assert lib.mica_w8a8_gemm_cfg(16, 32, 16, 32, 16, 16, None, 16, 0, 8, 4, 8, 32, 256, 256, 0, 2, None) == 1
     assert lib.mica_w8a8_gemm_swiglu_quant(16, 32, 16, 32, 16, 16, None, None, 16, 32, 16, 32, 16, 4, 32, 32, 0,
                                            16, 8, None) == 7                                   # workspace
     assert lib.mica_option_logits(16, 0, 64, None, 0, 1e-6, 16, 0, 64, None, None, 16, 16, 1, None) == 2

@@ -371,3 +371,36 @@ def test_gemm_into_column_slices_bit_exact(K):
         torch.ops.mica.w8a8_gemm_into(qx, sx, w, sw, None, out[:, lo:hi], 0)
         refs.append(torch.ops.mica.w8a8_gemm(qx, sx, w, sw, None, 0, 0))
     assert torch.equal(out, torch.cat(refs, dim=1))
+
+
+# ---------------------------------------------------------------------------------------
+# Split-K across a cluster (the K loop of one tile over S CTAs, partials summed in
+# distributed shared memory): every forced split factor is bit-exact.
+def _valid_split(k, s):
+    kb = (k + 127) // 128
+    per = (kb + s - 1) // s
+    return (s - 1) * per < kb
+
+
+@pytest.mark.parametrize('splits', [1, 2, 3, 5, 8])
+@pytest.mark.parametrize('bn', [64, 128, 256])
+@pytest.mark.parametrize('m,n,k', [(1, 256, 4096), (130, 320, 2560), (256, 2560, 9728), (77, 96, 1040)])
+def test_gemm_split_k_bit_exact(K, m, n, k, bn, splits):
+    if not _valid_split(k, splits):
+        pytest.skip('a rank would get no k-block')
+    g = torch.Generator().manual_seed(m + n + k + bn + splits)
+    lo = 31 if k > 1024 else 127                    # |acc| < 2^24: the fp32 output is the exact int32
+    qx = torch.randint(-lo, lo + 1, (m, k), generator=g, dtype=torch.int8)
+    qw = torch.randint(-lo, lo + 1, (n, k), generator=g, dtype=torch.int8)
+    tile = splits * 1000000 + 128000 + bn
+    y = torch.ops.mica.w8a8_gemm(qx.cuda(), torch.ones(m).cuda(), qw.cuda(), torch.ones(n).cuda(), None, 2, tile)
+    acc = O.int_gemm_exact(qx.numpy(), qw.numpy())
+    assert np.array_equal(y.cpu().numpy().astype(np.int64), acc.astype(np.int64))
+    # dequant epilogue with bias, bf16
+    sx = torch.rand(m, generator=g) * 0.05 + 1e-3
+    sw = torch.rand(n, generator=g) * 9e-3 + 1e-3
+    bias = torch.randn(n, generator=g) * 0.1
+    yb = torch.ops.mica.w8a8_gemm(qx.cuda(), sx.cuda(), qw.cuda(), sw.cuda(), bias.cuda(), 0, tile)
+    ref = O.dequant_out(acc, sx.numpy(), sw.numpy(), bias.numpy(), out='bf16')
+    assert np.array_equal(to_np(yb.float()), ref)
+    assert dev_error() == 0
