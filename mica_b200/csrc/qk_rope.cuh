@@ -120,28 +120,43 @@ __global__ void __launch_bounds__(256) qk_norm_rope_token_kernel(const QkRopeArg
     }
     __nv_bfloat16* row = a.qkv + s * a.ld;
     const int heads = a.H + a.KV;
-#pragma unroll 2
-    for (int h = 0; h < heads; ++h) {
-        __nv_bfloat16* x = row + static_cast<long>(h) * D;
-        const __nv_bfloat162 xl = *reinterpret_cast<const __nv_bfloat162*>(x + d);
-        const __nv_bfloat162 xh = *reinterpret_cast<const __nv_bfloat162*>(x + D / 2 + d);
-        const float2 fl = __bfloat1622float2(xl), fh = __bfloat1622float2(xh);
-        float ss = __fadd_rn(__fadd_rn(__fmul_rn(fl.x, fl.x), __fmul_rn(fl.y, fl.y)),
-                             __fadd_rn(__fmul_rn(fh.x, fh.x), __fmul_rn(fh.y, fh.y)));
-        ss = warp_sum(ss);
-        const float r = __frsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(D)), a.eps));
-        const bool is_q = h < a.H;
-        const float2 wl = __bfloat1622float2(is_q ? wq_lo : wk_lo), wh = __bfloat1622float2(is_q ? wq_hi : wk_hi);
-        const float2 cl = __bfloat1622float2(c_lo), ch = __bfloat1622float2(c_hi);
-        const float2 sl = __bfloat1622float2(s_lo), sh = __bfloat1622float2(s_hi);
-        const float yl0 = bf(__fmul_rn(wl.x, bf(__fmul_rn(fl.x, r)))), yl1 = bf(__fmul_rn(wl.y, bf(__fmul_rn(fl.y, r))));
-        const float yh0 = bf(__fmul_rn(wh.x, bf(__fmul_rn(fh.x, r)))), yh1 = bf(__fmul_rn(wh.y, bf(__fmul_rn(fh.y, r))));
-        const float ol0 = __fadd_rn(bf(__fmul_rn(yl0, cl.x)), bf(__fmul_rn(-yh0, sl.x)));
-        const float ol1 = __fadd_rn(bf(__fmul_rn(yl1, cl.y)), bf(__fmul_rn(-yh1, sl.y)));
-        const float oh0 = __fadd_rn(bf(__fmul_rn(yh0, ch.x)), bf(__fmul_rn(yl0, sh.x)));
-        const float oh1 = __fadd_rn(bf(__fmul_rn(yh1, ch.y)), bf(__fmul_rn(yl1, sh.y)));
-        *reinterpret_cast<__nv_bfloat162*>(x + d) = __floats2bfloat162_rn(ol0, ol1);
-        *reinterpret_cast<__nv_bfloat162*>(x + D / 2 + d) = __floats2bfloat162_rn(oh0, oh1);
+    // Eight heads are loaded before any is rewritten: the stores could alias later heads'
+    // loads, so without this the compiler keeps every load behind the previous head's store
+    // and the warp has one 256-byte request in flight.
+    constexpr int G = 8;
+    for (int h0 = 0; h0 < heads; h0 += G) {
+        __nv_bfloat162 xls[G], xhs[G];
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            if (h0 + g < heads) {
+                const __nv_bfloat16* x = row + static_cast<long>(h0 + g) * D;
+                xls[g] = *reinterpret_cast<const __nv_bfloat162*>(x + d);
+                xhs[g] = *reinterpret_cast<const __nv_bfloat162*>(x + D / 2 + d);
+            }
+        }
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            const int h = h0 + g;
+            if (h >= heads) break;                 // uniform across the warp
+            __nv_bfloat16* x = row + static_cast<long>(h) * D;
+            const float2 fl = __bfloat1622float2(xls[g]), fh = __bfloat1622float2(xhs[g]);
+            float ss = __fadd_rn(__fadd_rn(__fmul_rn(fl.x, fl.x), __fmul_rn(fl.y, fl.y)),
+                                 __fadd_rn(__fmul_rn(fh.x, fh.x), __fmul_rn(fh.y, fh.y)));
+            ss = warp_sum(ss);
+            const float r = __frsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(D)), a.eps));
+            const bool is_q = h < a.H;
+            const float2 wl = __bfloat1622float2(is_q ? wq_lo : wk_lo), wh = __bfloat1622float2(is_q ? wq_hi : wk_hi);
+            const float2 cl = __bfloat1622float2(c_lo), ch = __bfloat1622float2(c_hi);
+            const float2 sl = __bfloat1622float2(s_lo), sh = __bfloat1622float2(s_hi);
+            const float yl0 = bf(__fmul_rn(wl.x, bf(__fmul_rn(fl.x, r)))), yl1 = bf(__fmul_rn(wl.y, bf(__fmul_rn(fl.y, r))));
+            const float yh0 = bf(__fmul_rn(wh.x, bf(__fmul_rn(fh.x, r)))), yh1 = bf(__fmul_rn(wh.y, bf(__fmul_rn(fh.y, r))));
+            const float ol0 = __fadd_rn(bf(__fmul_rn(yl0, cl.x)), bf(__fmul_rn(-yh0, sl.x)));
+            const float ol1 = __fadd_rn(bf(__fmul_rn(yl1, cl.y)), bf(__fmul_rn(-yh1, sl.y)));
+            const float oh0 = __fadd_rn(bf(__fmul_rn(yh0, ch.x)), bf(__fmul_rn(yl0, sh.x)));
+            const float oh1 = __fadd_rn(bf(__fmul_rn(yh1, ch.y)), bf(__fmul_rn(yl1, sh.y)));
+            *reinterpret_cast<__nv_bfloat162*>(x + d) = __floats2bfloat162_rn(ol0, ol1);
+            *reinterpret_cast<__nv_bfloat162*>(x + D / 2 + d) = __floats2bfloat162_rn(oh0, oh1);
+        }
     }
 }
 
