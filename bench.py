@@ -323,11 +323,8 @@ def run_mica(args, rank, world, local):
     e2e_steps = max(1, min(args.steps, 5))
     e2e_ms = timed(e2e_step, e2e_steps, 1)
 
-    import torch.distributed as dist
-    t = torch.tensor([ms_total, e2e_ms, gemm_ms], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_total, e2e_ms, gemm_ms = t.tolist()
+    from mica_b200.shard import max_over_ranks
+    ms_total, e2e_ms, gemm_ms = max_over_ranks([ms_total, e2e_ms, gemm_ms], dev)
     extra = {}
     if not args.skip_model:
         extra['config2_chain'] = run_chain(dev)
@@ -444,36 +441,6 @@ def request_set(seed=4, n=256):
     return lengths, n_opts, ids
 
 
-def shard(lengths, world, rank):
-    """Greedy longest-processing-time split by cost ~ L + L^2 / 8192 (linears + attention)."""
-    cost = [int(L) + int(L) * int(L) / 8192.0 for L in lengths]
-    order = sorted(range(len(lengths)), key=lambda i: -cost[i])
-    load = [0.0] * world
-    mine = []
-    for i in order:
-        r = min(range(world), key=lambda j: load[j])
-        load[r] += cost[i]
-        if r == rank:
-            mine.append(i)
-    return sorted(mine)
-
-
-def plan_batches(lengths, batch_tokens):
-    """Groups request indices by sorted length so that (count x 64-token bucket of the
-    longest) stays within batch_tokens; a longer request goes alone."""
-    order = sorted(range(len(lengths)), key=lambda i: lengths[i])
-    out, cur = [], []
-    for i in order:
-        L = -(-lengths[i] // 64) * 64
-        if cur and (len(cur) + 1) * L > batch_tokens:
-            out.append(cur)
-            cur = []
-        cur.append(i)
-    if cur:
-        out.append(cur)
-    return out
-
-
 def run_prefill(dev, rank, world, batch_tokens=16384):
     """BASELINE configs 3 and 4 on a random-init 36-layer W8A8 decoder (4B dims, vocab 151936)."""
     import torch
@@ -502,8 +469,9 @@ def run_prefill(dev, rank, world, batch_tokens=16384):
                           'prob_sum': round(float(p.sum()), 6)}
     # config 4: 256 requests sharded over the ranks; each rank scores its share in batches of
     # similar length (sorted, padded to 64-token buckets, up to batch_tokens rows per pass)
+    from mica_b200.shard import lpt_shard, max_over_ranks, plan_batches
     lengths, n_opts, req_ids = request_set()
-    mine = shard(lengths, world, rank)
+    mine = lpt_shard(lengths, world, rank)
     batches = plan_batches([int(lengths[i]) for i in mine], batch_tokens)
     dev_ids = {i: torch.from_numpy(req_ids[i]).to(dev) for i in mine}
 
@@ -520,12 +488,10 @@ def run_prefill(dev, rank, world, batch_tokens=16384):
     run_batches()
     b.record()
     b.synchronize()
-    t = torch.tensor([a.elapsed_time(b)], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_box = max_over_ranks([a.elapsed_time(b)], dev)[0]
     total = int(lengths.sum())
-    out['config4_batch256'] = {'requests': len(lengths), 'tokens': total, 'ms_box': round(float(t.item()), 1),
-                               'tokens_per_s_box': round(total / float(t.item()) * 1e3),
+    out['config4_batch256'] = {'requests': len(lengths), 'tokens': total, 'ms_box': round(ms_box, 1),
+                               'tokens_per_s_box': round(total / ms_box * 1e3),
                                'batches_rank0': len(batches), 'batch_tokens': batch_tokens,
                                'sharding': f'LPT over {world} ranks, no collective'}
     pf.release()
