@@ -92,38 +92,40 @@ __device__ __forceinline__ void scale8(float (&f)[8], const float* inv) {
 }
 
 // Phase 2 of the fused SwiGLU kernel: each warp requantises whole rows of h [M, N/2] with
-// the row scale from the absmax that phase 1 accumulated (row_amax).
+// the row scale from the absmax that phase 1 accumulated (row_amax). Four 8-element vectors
+// per lane are loaded before any is used, so a warp keeps 4 KB of its row in flight.
 template <int MODE>
 __device__ __forceinline__ void swiglu_requant_rows(const GemmArgs& args, int warp, int lane) {
     const int I = args.N / 2;
     const int warps_total = gridDim.x * (blockDim.x >> 5);
+    constexpr int U = 4;
     for (int row = blockIdx.x * (blockDim.x >> 5) + warp; row < args.M; row += warps_total) {
         const unsigned bits = __ldcg(args.row_amax + row);
         const float scale = __fdiv_rn(fmaxf(__uint_as_float(bits), 1e-8f), 127.0f);
         const float rscale = __frcp_rn(scale);
         const __nv_bfloat16* hrow = args.h + static_cast<long>(row) * args.ldh;
         int8_t* qrow = args.q_out + static_cast<long>(row) * args.ldq;
-        // two 8-element vectors per lane per step: 16 independent divisions in flight
-        for (int c = lane * 8; c < I; c += 32 * 8 * 2) {
-            const int c2 = c + 32 * 8;
-            const bool has2 = c2 < I;
-            const uint4 v0 = __ldcg(reinterpret_cast<const uint4*>(hrow + c));
-            const uint4 v1 = has2 ? __ldcg(reinterpret_cast<const uint4*>(hrow + c2)) : make_uint4(0, 0, 0, 0);
-            float f0[8], f1[8];
-            const uint32_t w0[4] = {v0.x, v0.y, v0.z, v0.w}, w1[4] = {v1.x, v1.y, v1.z, v1.w};
+        for (int c0 = lane * 8; c0 < I; c0 += 32 * 8 * U) {
+            uint4 v[U];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                f0[2 * j] = __uint_as_float(w0[j] << 16);
-                f0[2 * j + 1] = __uint_as_float(w0[j] & 0xFFFF0000u);
-                f1[2 * j] = __uint_as_float(w1[j] << 16);
-                f1[2 * j + 1] = __uint_as_float(w1[j] & 0xFFFF0000u);
+            for (int u = 0; u < U; ++u) {
+                const int c = c0 + u * 32 * 8;
+                v[u] = c < I ? __ldcg(reinterpret_cast<const uint4*>(hrow + c)) : make_uint4(0, 0, 0, 0);
             }
-            if (args.inv_h != nullptr) {
-                scale8(f0, args.inv_h + c);
-                if (has2) scale8(f1, args.inv_h + c2);
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int c = c0 + u * 32 * 8;
+                if (c >= I) break;
+                float f[8];
+                const uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    f[2 * j] = __uint_as_float(w[j] << 16);
+                    f[2 * j + 1] = __uint_as_float(w[j] & 0xFFFF0000u);
+                }
+                if (args.inv_h != nullptr) scale8(f, args.inv_h + c);
+                *reinterpret_cast<uint2*>(qrow + c) = quant8<MODE>(f, scale, rscale);
             }
-            *reinterpret_cast<uint2*>(qrow + c) = quant8<MODE>(f0, scale, rscale);
-            if (has2) *reinterpret_cast<uint2*>(qrow + c2) = quant8<MODE>(f1, scale, rscale);
         }
         if (lane == 0) args.s_out[row] = scale;
     }
