@@ -13,8 +13,9 @@ value  : GEMM TOPS of the sweep, inputs resident in HBM, one CUDA-graph replay p
          timed with CUDA events (L2 flushed between steps by a 256 MiB write outside
          the timed events); whole-job = N x per-rank ops / max-over-ranks time.
 e2e    : the same sweep through the public API (QLinear-style calls) from pinned HOST
-         buffers, the H2D copy of every input and D2H copy of every output inside the
-         timed region.
+         buffers, the H2D copy of every distinct input and the D2H copy of every output
+         inside the timed region; copies run on two copy streams so both PCIe directions
+         overlap the kernels.
 roofline: the GEMM kernel alone (per-launch CUDA events, averaged over the sweep's
          shapes) against 2 x the measured bf16 dense peak (B200 dense int8 = 2 x bf16).
 other_configs: BASELINE config 2 (fused MLP chain, us per chain), config 3 (one 32k-token
@@ -304,24 +305,51 @@ def run_mica(args, rank, world, local):
             del g2
 
     # ---- e2e: host buffers through the public API, copies inside the timed region ----
+    # Each step copies its distinct inputs (one bf16 [M, K] per (M, K)) from pinned host memory
+    # on one copy stream, runs act_quant + mm_i8 as each input lands, and reads every result
+    # back on a second copy stream as soon as it is ready: the two PCIe directions and the
+    # kernels overlap, as a caller with pinned buffers and streams would run them.
     host_x = {key: t.cpu().pin_memory() for key, t in xs.items()}
+    dev_x = {key: torch.empty_like(t) for key, t in xs.items()}
     host_y = {}
     for m in MS:
         for name, n, k in PROJECTIONS:
             host_y[m, name] = torch.empty((m, n), dtype=torch.bfloat16).pin_memory()
-    h2d = sum(host_x[m, k].numel() * 2 for m in MS for _, _, k in PROJECTIONS)
+    h2d = sum(t.numel() * 2 for t in host_x.values())
     d2h = sum(t.numel() * 2 for t in host_y.values())
+    s_in, s_out = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+    order = []
+    for m in MS:
+        for _, _, k in PROJECTIONS:
+            if (m, k) not in order:
+                order.append((m, k))
 
     def e2e_step():
+        cur = torch.cuda.current_stream(dev)
+        s_in.wait_stream(cur)
+        s_out.wait_stream(cur)
+        landed = {}
+        with torch.cuda.stream(s_in):
+            for key in order:
+                dev_x[key].copy_(host_x[key], non_blocking=True)
+                landed[key] = torch.cuda.Event()
+                landed[key].record(s_in)
         for m in MS:
             for name, n, k in PROJECTIONS:
-                x = host_x[m, k].to(dev, non_blocking=True)
-                q, sc = K.act_quant(x, None)
+                cur.wait_event(landed[m, k])
+                q, sc = K.act_quant(dev_x[m, k], None)
                 y = K.mm_i8(q, sc, weights[name][0], weights[name][1], None, torch.bfloat16)
-                host_y[m, name].copy_(y, non_blocking=True)
+                done = torch.cuda.Event()
+                done.record(cur)
+                s_out.wait_event(done)
+                with torch.cuda.stream(s_out):
+                    host_y[m, name].copy_(y, non_blocking=True)
+                y.record_stream(s_out)
+        cur.wait_stream(s_in)
+        cur.wait_stream(s_out)
 
     e2e_steps = max(1, min(args.steps, 5))
-    e2e_ms = timed(e2e_step, e2e_steps, 1)
+    e2e_ms = timed(e2e_step, e2e_steps, 2)
 
     from mica_b200.shard import max_over_ranks
     ms_total, e2e_ms, gemm_ms = max_over_ranks([ms_total, e2e_ms, gemm_ms], dev)
