@@ -125,7 +125,9 @@ def tune(shapes, device='cuda', reps: int = 20, state_dir=None) -> dict:
     return out
 
 
-MODEL_SHAPES = ((6144, 2560), (2560, 4096), (19456, 2560), (2560, 9728), (2048, 2560), (4096, 2560))
+MODEL_SHAPES = ((6144, 2560), (2560, 4096), (19456, 2560), (2560, 9728), (2048, 2560), (4096, 2560),
+                # the Qwen3.5-4B hybrid's shapes (GDN a/b 32, k/v 1024, qkv 8192, FFN 9216)
+                (32, 2560), (1024, 2560), (8192, 2560), (9216, 2560), (2560, 9216))
 CLASS_M = (64, 256, 1024, 8192)     # one M per class s / m / n / l
 
 
