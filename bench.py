@@ -18,7 +18,8 @@ e2e    : the same sweep through the public API (QLinear-style calls) from pinned
          overlap the kernels.
 roofline: the GEMM kernel alone (per-launch CUDA events, averaged over the sweep's
          shapes) against 2 x the measured bf16 dense peak (B200 dense int8 = 2 x bf16).
-other_configs: BASELINE config 2 (fused MLP chain, us per chain), config 3 (one 32k-token
+other_configs: BASELINE config 0 (one linear at M=512, against both the tensor and the HBM
+         roofline), config 2 (fused MLP chain, us per chain), config 3 (one 32k-token
          request on a random-init 36-layer W8A8 decoder, tokens/s/GPU) and config 4 (256
          lognormal-length requests sharded over the ranks, tokens/s for the box).
 --impl reference: the reference's CPU path (the plain-C oracle's restatement of int8_quant
@@ -355,6 +356,7 @@ def run_mica(args, rank, world, local):
     ms_total, e2e_ms, gemm_ms = max_over_ranks([ms_total, e2e_ms, gemm_ms], dev)
     extra = {}
     if not args.skip_model:
+        extra['config0_linear'] = run_linear(dev)
         extra['config2_chain'] = run_chain(dev)
         extra.update(run_prefill(dev, rank, world))
     if rank != 0:
@@ -428,6 +430,38 @@ def run_chain(dev, reps=20):
     ops = 2 * M * 2 * I * H + 2 * M * H * I
     return {'config': 'config2: M=4096 RMSNorm+quant -> gate_up+SwiGLU+requant -> down', 'us_per_chain': round(us, 1),
             'gemm_tops': round(ops / us / 1e6, 1), 'launches_per_chain': 3}
+
+
+def run_linear(dev, reps=20):
+    """one W8A8 linear, M=512 K=2560 N=9728 (x N(0,1) bf16, per-token quant,
+    int8 weights, per-channel scales). Near the roofline ridge (~700 op/B), so the GEMM is
+    reported against both the int8 tensor peak and HBM."""
+    import torch
+    M, K_, N_ = 512, 2560, 9728
+    g = torch.Generator(device=dev).manual_seed(0)
+    x = torch.randn(M, K_, generator=g, device=dev).to(torch.bfloat16)
+    w = torch.randint(-127, 128, (N_, K_), generator=g, device=dev, dtype=torch.int8)
+    sw = torch.rand(N_, generator=g, device=dev) * 9e-3 + 1e-3
+    q, s = torch.ops.mica.act_quant(x, None, 0)
+
+    def linear():
+        qq, ss = torch.ops.mica.act_quant(x, None, 0)
+        return torch.ops.mica.w8a8_gemm(qq, ss, w, sw, None, 0, 0)
+
+    def gemm():
+        return torch.ops.mica.w8a8_gemm(q, s, w, sw, None, 0, 0)
+
+    us_lin = _graph_time(dev, linear, reps)
+    us_gemm = _graph_time(dev, gemm, reps)
+    ops = 2 * M * N_ * K_
+    gemm_bytes = M * K_ + N_ * K_ + 2 * M * N_ + 4 * (M + N_)
+    pk = peaks()
+    return {'config': 'config0: one linear M=512 K=2560 N=9728 (quant + GEMM)', 'us_per_linear': round(us_lin, 1),
+            'linear_tops': round(ops / us_lin / 1e6, 1), 'gemm_us': round(us_gemm, 1),
+            'gemm_tops': round(ops / us_gemm / 1e6, 1),
+            'gemm_frac_tensor': round(ops / us_gemm / 1e6 / (2 * pk['bf16']), 4),
+            'gemm_frac_hbm': round(gemm_bytes / us_gemm / 1e3 / pk['hbm'], 4),
+            'gemm_bytes': gemm_bytes, 'peaks': pk['source']}
 
 
 def _graph_time(dev, fn, reps):
