@@ -40,20 +40,37 @@ def lpt_shard(lengths, world: int, rank: int) -> list:
     return sorted(mine)
 
 
-def plan_batches(lengths, batch_tokens: int, bucket: int = 64) -> list:
-    """Groups request indices (into `lengths`) by ascending length so that count x the longest
-    request's bucket-rounded length stays within batch_tokens; a longer request goes alone."""
+# Fixed cost of one more batch (36 layers of launches, ramp-ups and tails), in tokens of work.
+# Fitted on B200 from two plans of the 256-request set: 34 batches with 6.0 % padding ran at
+# 178.6 K tokens/s and 52 batches with 2.1 % padding at 180.9 K, which puts one batch at ~625 tokens.
+BATCH_COST_TOKENS = 640
+
+
+def plan_batches(lengths, batch_tokens: int, bucket: int = 64, batch_cost: int = BATCH_COST_TOKENS) -> list:
+    """Groups request indices (into `lengths`) into padded [B, L] batches: contiguous runs of
+    the length-sorted requests, L = the longest rounded up to `bucket`, B x L <= batch_tokens
+    (a longer request goes alone). Among all such partitions it returns one that minimises the
+    rows computed (sum of B x L, padding included) plus `batch_cost` per batch: an exact
+    dynamic program over the sorted order, O(n^2) for n requests."""
     order = sorted(range(len(lengths)), key=lambda i: (lengths[i], i))
-    out, cur = [], []
-    for i in order:
-        padded = -(-int(lengths[i]) // bucket) * bucket
-        if cur and (len(cur) + 1) * padded > batch_tokens:
-            out.append(cur)
-            cur = []
-        cur.append(i)
-    if cur:
-        out.append(cur)
-    return out
+    n = len(order)
+    pad = [-(-int(lengths[i]) // bucket) * bucket for i in order]
+    inf = float('inf')
+    best = [0.0] + [inf] * n
+    cut = [0] * (n + 1)
+    for j in range(1, n + 1):
+        L = pad[j - 1]                   # the run [i, j) is padded to its longest, the last
+        for i in range(j - 1, -1, -1):
+            if j - i > 1 and (j - i) * L > batch_tokens:
+                break
+            c = best[i] + (j - i) * L + batch_cost
+            if c < best[j]:
+                best[j], cut[j] = c, i
+    out, j = [], n
+    while j > 0:
+        out.append([order[k] for k in range(cut[j], j)])
+        j = cut[j]
+    return out[::-1]
 
 
 def max_over_ranks(values, device='cpu'):

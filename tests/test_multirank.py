@@ -92,6 +92,30 @@ def test_two_gloo_ranks_partition_reduce_and_gather(tmp_path):
             assert len(b) == 1 or len(b) * pad <= 16384
 
 
+def test_batch_plan_minimises_padded_rows_plus_batch_cost():
+    """The planner's partition is never worse, on its own objective, than the greedy fill of
+    each batch up to the token budget, and respects the budget."""
+    lengths = _lengths(n=200, seed=11)
+    plan = SH.plan_batches(lengths, 16384)
+    assert sorted(i for b in plan for i in b) == list(range(len(lengths)))
+
+    def cost(batches):
+        return sum(len(b) * (-(-max(lengths[i] for i in b) // 64) * 64) + SH.BATCH_COST_TOKENS for b in batches)
+
+    order = sorted(range(len(lengths)), key=lambda i: (lengths[i], i))
+    greedy, cur = [], []
+    for i in order:
+        pad = -(-lengths[i] // 64) * 64
+        if cur and (len(cur) + 1) * pad > 16384:
+            greedy.append(cur)
+            cur = []
+        cur.append(i)
+    greedy.append(cur)
+    assert cost(plan) <= cost(greedy)
+    for b in plan:
+        assert len(b) == 1 or len(b) * (-(-max(lengths[i] for i in b) // 64) * 64) <= 16384
+
+
 def test_plan_is_the_single_process_plan():
     lengths = _lengths()
     assert SH.lpt_shard(lengths, 1, 0) == list(range(len(lengths)))
