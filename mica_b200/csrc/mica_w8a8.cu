@@ -409,8 +409,21 @@ int mica_device_error(int* code, void* stream) {
 }
 
 // ---------------------------------------------------------------------------------------
+template <typename T>
+static void norm_warp_launch(const QuantArgs& a, int nvec, cudaStream_t st) {
+    const dim3 grid(static_cast<unsigned>((a.M + 7) / 8)), block(256);
+    if (nvec <= 32 * 10) norm_rows_warp_kernel<T, 10><<<grid, block, 0, st>>>(a);
+    else norm_rows_warp_kernel<T, 16><<<grid, block, 0, st>>>(a);
+}
+
 static int quant_launch(const QuantArgs& a, int dtype, int kind, cudaStream_t st) {
     const int nvec = a.K / 8;
+    if (kind == QK_NORM && nvec <= 32 * 16 && (dtype == MICA_DT_BF16 || dtype == MICA_DT_FP16)) {
+        // rows up to 4096 wide: one warp per row (no block barriers)
+        if (dtype == MICA_DT_BF16) norm_warp_launch<__nv_bfloat16>(a, nvec, st);
+        else norm_warp_launch<__half>(a, nvec, st);
+        return launch_status();
+    }
     int threads = ((nvec + QV - 1) / QV + 31) / 32 * 32;
     if (threads < 32) threads = 32;
     if (threads > 1024) return MICA_ERR_UNSUPPORTED;

@@ -303,4 +303,136 @@ __global__ void __launch_bounds__(MAXT) quant_rows_kernel(const QuantArgs a) {
     if (threadIdx.x == 0) a.s[row] = scale;
 }
 
+// ---- residual add + RMSNorm + quantiser, one warp per row ----------------------------------
+// For rows up to 32 x 8 x MAXV elements (the 4B model's hidden 2560 needs MAXV = 10): no block
+// barriers, the row (after the residual add, rounded to T) stays packed in registers, and a
+// 256-thread block holds eight rows, so an SM keeps about 25 rows in flight instead of the ~11
+// of the block-per-row form. Same arithmetic per element as quant_rows_kernel<T, QK_NORM>; the
+// sum of squares runs per lane then over a warp tree (a different order than the block form).
+template <typename T>
+__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        if constexpr (std::is_same<T, __half>::value) {
+            __half2 h = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
+            w[i] = *reinterpret_cast<uint32_t*>(&h);
+        } else {
+            __nv_bfloat162 h = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+            w[i] = *reinterpret_cast<uint32_t*>(&h);
+        }
+    }
+    return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+template <typename T, int MAXV, int MODE>
+__device__ __forceinline__ void norm_row_warp(const QuantArgs& a, long row, int lane) {
+    const int nvec = a.K >> 3;
+    // distinct buffers: restrict lets the compiler issue later vectors' loads ahead of
+    // earlier vectors' stores
+    const T* __restrict__ xr = static_cast<const T*>(a.x) + row * a.ldx;
+    T* __restrict__ sum_row = a.sum_out ? static_cast<T*>(a.sum_out) + row * a.ldsum : nullptr;
+    T* __restrict__ y_row = a.y_out ? static_cast<T*>(a.y_out) + row * a.ldy : nullptr;
+    const T* __restrict__ gp = static_cast<const T*>(a.gamma);
+    const float* __restrict__ inv = a.inv;
+    uint4 v[MAXV];
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+        const int idx = lane + 32 * i;
+        v[i] = idx < nvec ? __ldg(reinterpret_cast<const uint4*>(xr + idx * 8)) : make_uint4(0u, 0u, 0u, 0u);
+    }
+    if (a.residual != nullptr) {
+        const T* __restrict__ rr = static_cast<const T*>(a.residual) + row * a.ldr;
+        uint4 rv[MAXV];
+#pragma unroll
+        for (int i = 0; i < MAXV; ++i) {
+            const int idx = lane + 32 * i;
+            rv[i] = idx < nvec ? __ldg(reinterpret_cast<const uint4*>(rr + idx * 8)) : make_uint4(0u, 0u, 0u, 0u);
+        }
+#pragma unroll
+        for (int i = 0; i < MAXV; ++i) {
+            const int idx = lane + 32 * i;
+            if (idx < nvec) {
+                float f[8], r[8];
+                unpack8<T>(v[i], f);
+                unpack8<T>(rv[i], r);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) f[e] = __fadd_rn(f[e], r[e]);   // rounded to T by the pack
+                v[i] = pack8<T>(f);
+                if (sum_row != nullptr) *reinterpret_cast<uint4*>(sum_row + idx * 8) = v[i];
+            }
+        }
+    }
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+        if (lane + 32 * i < nvec) {
+            float f[8];
+            unpack8<T>(v[i], f);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) ss = __fadd_rn(ss, __fmul_rn(f[e], f[e]));
+        }
+    }
+    ss = warp_sum(ss);
+    const float rs = __frsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(a.K)), a.eps));
+    float am = 0.f;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+        const int idx = lane + 32 * i;
+        if (idx < nvec) {
+            float f[8], w[8];
+            unpack8<T>(v[i], f);
+            unpack8<T>(__ldg(reinterpret_cast<const uint4*>(gp + idx * 8)), w);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const float n = __fmul_rn(f[e], rs);
+                f[e] = a.norm_style == MICA_NORM_OFFSET ? round_to<T>(__fmul_rn(n, __fadd_rn(1.0f, w[e])))
+                                                        : round_to<T>(__fmul_rn(w[e], round_to<T>(n)));
+            }
+            v[i] = pack8<T>(f);
+            if (y_row != nullptr) *reinterpret_cast<uint4*>(y_row + idx * 8) = v[i];
+            if (inv != nullptr) {
+                const float4 i0 = __ldg(reinterpret_cast<const float4*>(inv + idx * 8));
+                const float4 i1 = __ldg(reinterpret_cast<const float4*>(inv + idx * 8) + 1);
+                const float iv[8] = {i0.x, i0.y, i0.z, i0.w, i1.x, i1.y, i1.z, i1.w};
+#pragma unroll
+                for (int e = 0; e < 8; ++e) f[e] = __fmul_rn(f[e], iv[e]);
+            }
+#pragma unroll
+            for (int e = 0; e < 8; ++e) am = fmaxf(am, fabsf(f[e]));
+        }
+    }
+    if (a.q == nullptr) return;          // norm-only call
+    am = warp_max(am);
+    const float scale = __fdiv_rn(fmaxf(am, 1e-8f), 127.0f);
+    const float rscale = __frcp_rn(scale);
+    int8_t* qr = a.q + row * a.ldq;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+        const int idx = lane + 32 * i;
+        if (idx < nvec) {
+            float f[8];
+            unpack8<T>(v[i], f);
+            if (inv != nullptr) {
+                const float4 i0 = __ldg(reinterpret_cast<const float4*>(inv + idx * 8));
+                const float4 i1 = __ldg(reinterpret_cast<const float4*>(inv + idx * 8) + 1);
+                const float iv[8] = {i0.x, i0.y, i0.z, i0.w, i1.x, i1.y, i1.z, i1.w};
+#pragma unroll
+                for (int e = 0; e < 8; ++e) f[e] = __fmul_rn(f[e], iv[e]);
+            }
+            *reinterpret_cast<uint2*>(qr + idx * 8) = quant8<MODE>(f, scale, rscale);
+        }
+    }
+    if (lane == 0) a.s[row] = scale;
+}
+
+template <typename T, int MAXV>
+__global__ void __launch_bounds__(256) norm_rows_warp_kernel(const QuantArgs a) {
+    const long row = (static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (row >= a.M) return;
+    if (a.round_mode == MICA_ROUND_HALF_EVEN) norm_row_warp<T, MAXV, MICA_ROUND_HALF_EVEN>(a, row, lane);
+    else norm_row_warp<T, MAXV, MICA_ROUND_HALF_AWAY>(a, row, lane);
+}
+
 }  // namespace mica
