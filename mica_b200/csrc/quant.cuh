@@ -139,7 +139,7 @@ __device__ __forceinline__ void unpack8(const uint4& w, float (&f)[8]) {
 
 // mica_act_quant on 16-bit input without a smoothing vector: the row stays packed in
 // registers (half the registers of the fp32 copy) and the absmax runs on packed pairs.
-template <typename T, int MODE>
+template <typename T, int MODE, int QV = mica::QV>
 __device__ __forceinline__ void quant_row_packed(const QuantArgs& a, float* red) {
     const int row = blockIdx.x;
     const int nvec = a.K >> 3;
@@ -301,6 +301,16 @@ __global__ void __launch_bounds__(MAXT) quant_rows_kernel(const QuantArgs a) {
     if (a.round_mode == MICA_ROUND_HALF_EVEN) store_codes<MICA_ROUND_HALF_EVEN>(v, nvec, scale, rscale, qr);
     else store_codes<MICA_ROUND_HALF_AWAY>(v, nvec, scale, rscale, qr);
     if (threadIdx.x == 0) a.s[row] = scale;
+}
+
+// mica_act_quant on 16-bit rows without a smoothing vector, QVP vectors of 8 elements per
+// thread (quant_row_packed): wide rows take 8 per thread, so a row needs half the threads,
+// its two reductions are shallower and more rows fit on an SM.
+template <typename T, int QVP>
+__global__ void __launch_bounds__(512) quant_rows_packed_kernel(const QuantArgs a) {
+    __shared__ float red[32];
+    if (a.round_mode == MICA_ROUND_HALF_EVEN) quant_row_packed<T, MICA_ROUND_HALF_EVEN, QVP>(a, red);
+    else quant_row_packed<T, MICA_ROUND_HALF_AWAY, QVP>(a, red);
 }
 
 // ---- residual add + RMSNorm + quantiser, one warp per row ----------------------------------
