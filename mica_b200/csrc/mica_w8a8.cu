@@ -411,7 +411,7 @@ int mica_device_error(int* code, void* stream) {
 // ---------------------------------------------------------------------------------------
 template <typename T>
 static void norm_warp_launch(const QuantArgs& a, int nvec, cudaStream_t st) {
-    const dim3 grid(static_cast<unsigned>((a.M + 7) / 8)), block(256);
+    const dim3 grid(static_cast<unsigned>((a.M + 3) / 4)), block(128);
     if (nvec <= 32 * 10) norm_rows_warp_kernel<T, 10><<<grid, block, 0, st>>>(a);
     else norm_rows_warp_kernel<T, 16><<<grid, block, 0, st>>>(a);
 }

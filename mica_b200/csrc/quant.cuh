@@ -316,8 +316,8 @@ __global__ void __launch_bounds__(512) quant_rows_packed_kernel(const QuantArgs 
 // ---- residual add + RMSNorm + quantiser, one warp per row ----------------------------------
 // For rows up to 32 x 8 x MAXV elements (the 4B model's hidden 2560 needs MAXV = 10): no block
 // barriers, the row (after the residual add, rounded to T) stays packed in registers, and a
-// 256-thread block holds eight rows, so an SM keeps about 25 rows in flight instead of the ~11
-// of the block-per-row form. Same arithmetic per element as quant_rows_kernel<T, QK_NORM>; the
+// 128-thread block holds four rows, and up to 2560-wide rows are held to 96 registers so that
+// five blocks (20 rows) fit on an SM, against ~11 rows for the block-per-row form. Same arithmetic per element as quant_rows_kernel<T, QK_NORM>; the
 // sum of squares runs per lane then over a warp tree (a different order than the block form).
 template <typename T>
 __device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
@@ -437,7 +437,7 @@ __device__ __forceinline__ void norm_row_warp(const QuantArgs& a, long row, int 
 }
 
 template <typename T, int MAXV>
-__global__ void __launch_bounds__(256) norm_rows_warp_kernel(const QuantArgs a) {
+__global__ void __launch_bounds__(128, MAXV <= 10 ? 5 : 3) norm_rows_warp_kernel(const QuantArgs a) {
     const long row = (static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (row >= a.M) return;
