@@ -204,6 +204,25 @@ def test_rmsnorm_quant_golden(K, case):
     assert ulp.max() <= 1 and (ulp > 0).mean() < 0.01
 
 
+@pytest.mark.parametrize('k', [1024, 4096, 8192])
+def test_rmsnorm_quant_widths(K, k):
+    """Rows up to 4096 wide take the warp-per-row kernel (two register sizings), wider rows the
+    block-per-row kernel; both against the oracle, with a residual and the summed stream."""
+    m = 300
+    g = torch.Generator().manual_seed(k)
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16)
+    r = torch.randn(m, k, generator=g).to(torch.bfloat16)
+    gam = (1 + 0.1 * torch.randn(k, generator=g)).to(torch.bfloat16)
+    q, s, y, summed = K.rmsnorm_quant(x.cuda(), gam.cuda(), 1e-6, r.cuda(), style=1, want_y=True)
+    yo, so = O.rms_norm(x.float().numpy(), gam.float().numpy(), 1e-6, r.float().numpy(), style='weight')
+    assert np.array_equal(to_np(summed), so)
+    yk = to_np(y)
+    ulp = np.abs(O.f32_to_bf16_bits(yk).astype(int) - O.f32_to_bf16_bits(yo).astype(int))
+    assert ulp.max() <= 2 and (ulp > 0).mean() < 0.01
+    q2, s2 = O.quant_act_half_away(yk)
+    assert np.array_equal(q.cpu().numpy(), q2) and np.array_equal(s.cpu().numpy(), s2)
+
+
 @pytest.mark.parametrize('m', [1, 33, 4096])
 def test_rmsnorm_quant_outliers(K, m):
     k = 2560
