@@ -92,13 +92,14 @@ __device__ __forceinline__ void scale8(float (&f)[8], const float* inv) {
 }
 
 // Phase 2 of the fused SwiGLU kernel: each warp requantises whole rows of h [M, N/2] with
-// the row scale from the absmax that phase 1 accumulated (row_amax). Four 8-element vectors
-// per lane are loaded before any is used, so a warp keeps 4 KB of its row in flight.
+// the row scale from the absmax that phase 1 accumulated (row_amax). Eight 8-element vectors
+// per lane are loaded before any is used, so a warp keeps 8 KB of its row in flight: phase 2
+// runs on the GEMM's ten warps per SM, and the bytes in flight set its bandwidth.
 template <int MODE>
 __device__ __forceinline__ void swiglu_requant_rows(const GemmArgs& args, int warp, int lane) {
     const int I = args.N / 2;
     const int warps_total = gridDim.x * (blockDim.x >> 5);
-    constexpr int U = 4;
+    constexpr int U = 8;
     for (int row = blockIdx.x * (blockDim.x >> 5) + warp; row < args.M; row += warps_total) {
         const unsigned bits = __ldcg(args.row_amax + row);
         const float scale = __fdiv_rn(fmaxf(__uint_as_float(bits), 1e-8f), 127.0f);
