@@ -779,7 +779,8 @@ int mica_qk_norm_rope(void* qkv, long ld, const void* q_w, const void* k_w, cons
     if (!qkv || !cos || !sin || (H > 0 && !q_w) || (KV > 0 && !k_w)) return MICA_ERR_ARG;
     if (S < 0 || H < 0 || KV < 0 || (D != 64 && D != 128) || ld < static_cast<long>(H + KV) * D || pos0 < 0)
         return MICA_ERR_SHAPE;
-    if (!aligned16(qkv) || (ld * 2) % 16) return MICA_ERR_ALIGN;
+    const auto al8 = [](const void* ptr) { return ptr == nullptr || reinterpret_cast<uintptr_t>(ptr) % 8 == 0; };
+    if (!aligned16(qkv) || (ld * 2) % 16 || !al8(cos) || !al8(sin) || !al8(q_w) || !al8(k_w)) return MICA_ERR_ALIGN;
     int rc = check_device(nullptr);
     if (rc) return rc;
     const long warps = static_cast<long>(S) * (H + KV);

@@ -94,68 +94,89 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(const QkRopeArgs a) {
     }
 }
 
-// One warp per token for D = 128: lane l owns dims (2l, 2l+1) and their rotation partners
-// (64+2l, 64+2l+1). cos/sin of the token and both norm weights stay in registers across the
-// token's H + KV heads; each head costs two 4-byte loads and stores per lane. Every step is
-// fp32 arithmetic followed by an explicit bf16 rounding, the HF op sequence.
+// One warp per token for D = 128, two heads at a time: half-warp p (lanes 16p..16p+15) takes
+// head h0 + p, and its lane j owns dims [4j, 4j+4) and their rotation partners [64+4j, 64+4j+4).
+// cos/sin of the token and both norm weights stay in registers across the token's H + KV
+// heads; each head costs a lane two 8-byte loads and stores, and one 4-step shuffle sequence
+// reduces both heads' sums of squares. Eight heads are loaded before any is rewritten (a store
+// could alias a later head's load, which would otherwise serialise them). Every step is fp32
+// arithmetic followed by an explicit bf16 rounding, the HF op sequence.
+__device__ __forceinline__ void unpack4_bf16(const uint2 w, float (&f)[4]) {
+    f[0] = __uint_as_float(w.x << 16);
+    f[1] = __uint_as_float(w.x & 0xFFFF0000u);
+    f[2] = __uint_as_float(w.y << 16);
+    f[3] = __uint_as_float(w.y & 0xFFFF0000u);
+}
+
 __global__ void __launch_bounds__(256) qk_norm_rope_token_kernel(const QkRopeArgs a) {
     constexpr int D = 128;
     const long s = (static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (s >= a.S) return;
+    const int half = lane >> 4;
+    const int d = 4 * (lane & 15);
     const long p = a.pos ? a.pos[s] : a.pos0 + s;
-    const int d = 2 * lane;
-    const __nv_bfloat162 c_lo = *reinterpret_cast<const __nv_bfloat162*>(a.cos + p * D + d);
-    const __nv_bfloat162 c_hi = *reinterpret_cast<const __nv_bfloat162*>(a.cos + p * D + D / 2 + d);
-    const __nv_bfloat162 s_lo = *reinterpret_cast<const __nv_bfloat162*>(a.sin + p * D + d);
-    const __nv_bfloat162 s_hi = *reinterpret_cast<const __nv_bfloat162*>(a.sin + p * D + D / 2 + d);
-    __nv_bfloat162 wq_lo = __float2bfloat162_rn(0.f), wq_hi = wq_lo, wk_lo = wq_lo, wk_hi = wq_lo;
+    float cl[4], ch[4], sl[4], sh[4], wql[4] = {}, wqh[4] = {}, wkl[4] = {}, wkh[4] = {};
+    unpack4_bf16(*reinterpret_cast<const uint2*>(a.cos + p * D + d), cl);
+    unpack4_bf16(*reinterpret_cast<const uint2*>(a.cos + p * D + D / 2 + d), ch);
+    unpack4_bf16(*reinterpret_cast<const uint2*>(a.sin + p * D + d), sl);
+    unpack4_bf16(*reinterpret_cast<const uint2*>(a.sin + p * D + D / 2 + d), sh);
     if (a.H > 0) {
-        wq_lo = *reinterpret_cast<const __nv_bfloat162*>(a.q_w + d);
-        wq_hi = *reinterpret_cast<const __nv_bfloat162*>(a.q_w + D / 2 + d);
+        unpack4_bf16(*reinterpret_cast<const uint2*>(a.q_w + d), wql);
+        unpack4_bf16(*reinterpret_cast<const uint2*>(a.q_w + D / 2 + d), wqh);
     }
     if (a.KV > 0) {
-        wk_lo = *reinterpret_cast<const __nv_bfloat162*>(a.k_w + d);
-        wk_hi = *reinterpret_cast<const __nv_bfloat162*>(a.k_w + D / 2 + d);
+        unpack4_bf16(*reinterpret_cast<const uint2*>(a.k_w + d), wkl);
+        unpack4_bf16(*reinterpret_cast<const uint2*>(a.k_w + D / 2 + d), wkh);
     }
     __nv_bfloat16* row = a.qkv + s * a.ld;
     const int heads = a.H + a.KV;
-    // Eight heads are loaded before any is rewritten: the stores could alias later heads'
-    // loads, so without this the compiler keeps every load behind the previous head's store
-    // and the warp has one 256-byte request in flight.
-    constexpr int G = 8;
-    for (int h0 = 0; h0 < heads; h0 += G) {
-        __nv_bfloat162 xls[G], xhs[G];
+    constexpr int G = 4;                          // head pairs loaded ahead
+    for (int h0 = 0; h0 < heads; h0 += 2 * G) {
+        uint2 xl[G], xh[G];
 #pragma unroll
         for (int g = 0; g < G; ++g) {
-            if (h0 + g < heads) {
-                const __nv_bfloat16* x = row + static_cast<long>(h0 + g) * D;
-                xls[g] = *reinterpret_cast<const __nv_bfloat162*>(x + d);
-                xhs[g] = *reinterpret_cast<const __nv_bfloat162*>(x + D / 2 + d);
+            const int h = h0 + 2 * g + half;
+            if (h < heads) {
+                const __nv_bfloat16* x = row + static_cast<long>(h) * D;
+                xl[g] = *reinterpret_cast<const uint2*>(x + d);
+                xh[g] = *reinterpret_cast<const uint2*>(x + D / 2 + d);
+            } else {
+                xl[g] = xh[g] = make_uint2(0u, 0u);
             }
         }
 #pragma unroll
         for (int g = 0; g < G; ++g) {
-            const int h = h0 + g;
-            if (h >= heads) break;                 // uniform across the warp
-            __nv_bfloat16* x = row + static_cast<long>(h) * D;
-            const float2 fl = __bfloat1622float2(xls[g]), fh = __bfloat1622float2(xhs[g]);
-            float ss = __fadd_rn(__fadd_rn(__fmul_rn(fl.x, fl.x), __fmul_rn(fl.y, fl.y)),
-                                 __fadd_rn(__fmul_rn(fh.x, fh.x), __fmul_rn(fh.y, fh.y)));
-            ss = warp_sum(ss);
+            if (h0 + 2 * g >= heads) break;       // uniform across the warp
+            const int h = h0 + 2 * g + half;
+            float fl[4], fh[4];
+            unpack4_bf16(xl[g], fl);
+            unpack4_bf16(xh[g], fh);
+            float ss = 0.f;
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+                ss = __fadd_rn(ss, __fadd_rn(__fmul_rn(fl[e], fl[e]), __fmul_rn(fh[e], fh[e])));
+#pragma unroll
+            for (int o = 8; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+            if (h >= heads) continue;
             const float r = __frsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(D)), a.eps));
             const bool is_q = h < a.H;
-            const float2 wl = __bfloat1622float2(is_q ? wq_lo : wk_lo), wh = __bfloat1622float2(is_q ? wq_hi : wk_hi);
-            const float2 cl = __bfloat1622float2(c_lo), ch = __bfloat1622float2(c_hi);
-            const float2 sl = __bfloat1622float2(s_lo), sh = __bfloat1622float2(s_hi);
-            const float yl0 = bf(__fmul_rn(wl.x, bf(__fmul_rn(fl.x, r)))), yl1 = bf(__fmul_rn(wl.y, bf(__fmul_rn(fl.y, r))));
-            const float yh0 = bf(__fmul_rn(wh.x, bf(__fmul_rn(fh.x, r)))), yh1 = bf(__fmul_rn(wh.y, bf(__fmul_rn(fh.y, r))));
-            const float ol0 = __fadd_rn(bf(__fmul_rn(yl0, cl.x)), bf(__fmul_rn(-yh0, sl.x)));
-            const float ol1 = __fadd_rn(bf(__fmul_rn(yl1, cl.y)), bf(__fmul_rn(-yh1, sl.y)));
-            const float oh0 = __fadd_rn(bf(__fmul_rn(yh0, ch.x)), bf(__fmul_rn(yl0, sh.x)));
-            const float oh1 = __fadd_rn(bf(__fmul_rn(yh1, ch.y)), bf(__fmul_rn(yl1, sh.y)));
-            *reinterpret_cast<__nv_bfloat162*>(x + d) = __floats2bfloat162_rn(ol0, ol1);
-            *reinterpret_cast<__nv_bfloat162*>(x + D / 2 + d) = __floats2bfloat162_rn(oh0, oh1);
+            float ol[4], oh[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float wl = is_q ? wql[e] : wkl[e], wh = is_q ? wqh[e] : wkh[e];
+                const float yl = bf(__fmul_rn(wl, bf(__fmul_rn(fl[e], r))));
+                const float yh = bf(__fmul_rn(wh, bf(__fmul_rn(fh[e], r))));
+                ol[e] = __fadd_rn(bf(__fmul_rn(yl, cl[e])), bf(__fmul_rn(-yh, sl[e])));
+                oh[e] = __fadd_rn(bf(__fmul_rn(yh, ch[e])), bf(__fmul_rn(yl, sh[e])));
+            }
+            __nv_bfloat16* x = row + static_cast<long>(h) * D;
+            const __nv_bfloat162 l0 = __floats2bfloat162_rn(ol[0], ol[1]), l1 = __floats2bfloat162_rn(ol[2], ol[3]);
+            const __nv_bfloat162 g0 = __floats2bfloat162_rn(oh[0], oh[1]), g1 = __floats2bfloat162_rn(oh[2], oh[3]);
+            *reinterpret_cast<uint2*>(x + d) = make_uint2(*reinterpret_cast<const uint32_t*>(&l0),
+                                                          *reinterpret_cast<const uint32_t*>(&l1));
+            *reinterpret_cast<uint2*>(x + D / 2 + d) = make_uint2(*reinterpret_cast<const uint32_t*>(&g0),
+                                                                  *reinterpret_cast<const uint32_t*>(&g1));
         }
     }
 }
