@@ -137,8 +137,9 @@ __device__ __forceinline__ void unpack8(const uint4& w, float (&f)[8]) {
     }
 }
 
-// mica_act_quant on 16-bit input without a smoothing vector: the row stays packed in
-// registers (half the registers of the fp32 copy) and the absmax runs on packed pairs.
+// mica_act_quant on 16-bit input without a smoothing vector (quant_rows_packed_kernel): the
+// row stays packed in registers (half the registers of an fp32 copy) and the absmax runs on
+// packed pairs.
 template <typename T, int MODE, int QV = mica::QV>
 __device__ __forceinline__ void quant_row_packed(const QuantArgs& a, float* red) {
     const int row = blockIdx.x;
@@ -189,13 +190,6 @@ template <typename T, int KIND, int MAXT = 512>
 __global__ void __launch_bounds__(MAXT) quant_rows_kernel(const QuantArgs a) {
     constexpr bool NORM = KIND == QK_NORM;
     __shared__ float red[32];
-    if constexpr (KIND == QK_PLAIN && sizeof(T) == 2) {
-        if (a.inv == nullptr) {
-            if (a.round_mode == MICA_ROUND_HALF_EVEN) quant_row_packed<T, MICA_ROUND_HALF_EVEN>(a, red);
-            else quant_row_packed<T, MICA_ROUND_HALF_AWAY>(a, red);
-            return;
-        }
-    }
     const int row = blockIdx.x;
     const int nvec = a.K >> 3;
     const T* xr = static_cast<const T*>(a.x) + static_cast<long>(row) * a.ldx;
@@ -314,11 +308,12 @@ __global__ void __launch_bounds__(512) quant_rows_packed_kernel(const QuantArgs 
 }
 
 // ---- residual add + RMSNorm + quantiser, one warp per row ----------------------------------
-// For rows up to 32 x 8 x MAXV elements (the 4B model's hidden 2560 needs MAXV = 10): no block
-// barriers, the row (after the residual add, rounded to T) stays packed in registers, and a
-// 128-thread block holds four rows, and up to 2560-wide rows are held to 96 registers so that
-// five blocks (20 rows) fit on an SM, against ~11 rows for the block-per-row form. Same arithmetic per element as quant_rows_kernel<T, QK_NORM>; the
-// sum of squares runs per lane then over a warp tree (a different order than the block form).
+// For rows up to 32 x 8 x MAXV elements (the 4B model's hidden 2560 needs MAXV = 10). No block
+// barriers: the row (after the residual add, rounded to T) stays packed in registers, a
+// 128-thread block holds four rows, and rows up to 2560 wide are held to 96 registers so that
+// five blocks (20 rows) fit on an SM, against ~11 rows for the block-per-row form. Same
+// arithmetic per element as quant_rows_kernel<T, QK_NORM>; the sum of squares runs per lane,
+// then over a warp tree (a different order than the block form).
 template <typename T>
 __device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
     uint32_t w[4];
