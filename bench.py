@@ -542,7 +542,12 @@ def run_prefill(dev, rank, world, batch_tokens=16384):
             reqs = [mine[j] for j in bt]
             pf.score_batch([dev_ids[i] for i in reqs], [(2, 2 + int(n_opts[i])) for i in reqs])
 
-    run_batches()         # warm-up pass over every batch shape (as a server warms up at start)
+    # start-up, as a server warms up for its batch shapes: one graph per [B, L] in the plan,
+    # then a warm-up pass over every batch
+    shapes = sorted({(len(bt), pf.bucket(max(int(lengths[mine[j]]) for j in bt))) for bt in batches})
+    for B, L in shapes:
+        pf.capture_batch(B, L)
+    run_batches()
     torch.cuda.synchronize(dev)
     if world > 1:
         dist.barrier()
@@ -554,7 +559,8 @@ def run_prefill(dev, rank, world, batch_tokens=16384):
     total = int(lengths.sum())
     out['config4_batch256'] = {'requests': len(lengths), 'tokens': total, 'ms_box': round(ms_box, 1),
                                'tokens_per_s_box': round(total / ms_box * 1e3),
-                               'batches_rank0': len(batches), 'batch_tokens': batch_tokens,
+                               'batches_rank0': len(batches), 'batch_graphs_rank0': len(shapes),
+                               'batch_tokens': batch_tokens,
                                'sharding': f'LPT over {world} ranks, no collective'}
     pf.release()
     del model, pf

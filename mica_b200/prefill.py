@@ -23,7 +23,8 @@ scored row (prefill_engine.py:306-339), then the fused final norm + gathered lm_
 
 Graphs: capture() records the whole prefill for a 64-token bucket with a static id
 buffer and a `limit` row (the real length), like the reference's per-bucket graphs; rows
-past `limit` are padding that no real row attends to.
+past `limit` are padding that no real row attends to. capture_batch() does the same for a
+padded [B, L] batch (per-request limits and option slices), like the reference's batch graphs.
 """
 from __future__ import annotations
 
@@ -376,6 +377,7 @@ class Prefill:
         self.max_len = max_len
         self.scale = cfg.head_dim ** -0.5
         self.graphs = {}
+        self.batch_graphs = {}
         self.pool = None
         self._pos = {}
         if attn_backends is None:
@@ -546,24 +548,66 @@ class Prefill:
         return self.probs(self.hidden_last(ids, limit), lo_t, hi_t)
 
     @torch.no_grad()
-    def score_batch(self, ids_list, slices=None):
+    def score_batch(self, ids_list, slices=None, graphs: bool = True):
         """Scores several requests in one pass: ids padded to [B, L] (L a multiple of 64),
         each request's own length as its limit, per-request option slices (lo, hi).
         Returns (logits, probs) fp32 [B, n_rows]. Used for batches of similar lengths, like
-        the reference's shaped batching (v0.5/serving/lib/release_runtime.py:1156-1227)."""
+        the reference's shaped batching (v0.5/serving/lib/release_runtime.py:1156-1227); a
+        [B, L] shape with a captured graph (capture_batch) replays it, like the reference's
+        batch graphs (release_runtime.py:644-647). The per-request lengths and slices travel
+        in one pinned copy, so nothing here waits for the device."""
         dev = self.m.device
         B = len(ids_list)
         lens = [int(t.shape[0]) for t in ids_list]
         L = self.bucket(max(lens))
-        ids = torch.zeros(B, L, dtype=torch.long, device=dev)
+        rows = self.rows.shape[0]
+        sl = slices if slices is not None else [(0, rows)] * B
+        meta = torch.tensor(lens + [int(a) for a, _ in sl] + [int(b) for _, b in sl], dtype=torch.long)
+        meta = meta.pin_memory().to(dev, non_blocking=True)
+        e = self.batch_graphs.get((B, L)) if graphs else None
+        if e is None:
+            ids = torch.zeros(B, L, dtype=torch.long, device=dev)
+            limit = meta[:B]
+            lo, hi = (None, None) if slices is None else (meta[B:2 * B].int(), meta[2 * B:].int())
+        else:
+            ids, limit, lo, hi = e['ids'], e['limit'], e['lo'], e['hi']
+            ids.zero_()
+            limit.copy_(meta[:B])
+            lo.copy_(meta[B:2 * B])
+            hi.copy_(meta[2 * B:])
         for i, t in enumerate(ids_list):
             ids[i, :lens[i]].copy_(t)
-        limit = torch.tensor(lens, dtype=torch.long, device=dev)
-        lo = hi = None
-        if slices is not None:
-            lo = torch.tensor([int(a) for a, _ in slices], dtype=torch.int32, device=dev)
-            hi = torch.tensor([int(b) for _, b in slices], dtype=torch.int32, device=dev)
-        return self.probs(self.hidden_last(ids, limit), lo, hi)
+        if e is None:
+            return self.probs(self.hidden_last(ids, limit), lo, hi)
+        e['graph'].replay()
+        return e['out'][0].clone(), e['out'][1].clone()
+
+    @torch.no_grad()
+    def capture_batch(self, B: int, L: int):
+        """Captures the prefill of a padded [B, L] batch (L a multiple of 64) with static ids,
+        per-request limits and option slices; score_batch replays it for that shape. The
+        reference's capture_batch (v0.5/serving/lib/release_runtime.py:670-689) keys its batch
+        graphs the same way."""
+        if L % BUCKET or L > self.max_len or B < 1:
+            raise ValueError(f'batch shape {B} x {L}: L must be a multiple of {BUCKET} within {self.max_len}')
+        dev = self.m.device
+        ids = torch.zeros(B, L, dtype=torch.long, device=dev)
+        limit = torch.full((B,), L, dtype=torch.long, device=dev)
+        lo = torch.zeros(B, dtype=torch.int32, device=dev)
+        hi = torch.full((B,), self.rows.shape[0], dtype=torch.int32, device=dev)
+        s = torch.cuda.Stream(device=dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                self.probs(self.hidden_last(ids, limit), lo, hi)
+        torch.cuda.current_stream(dev).wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        if self.pool is None:
+            self.pool = torch.cuda.graph_pool_handle()
+        with torch.cuda.graph(g, pool=self.pool):
+            out = self.probs(self.hidden_last(ids, limit), lo, hi)
+        self.batch_graphs[B, L] = {'graph': g, 'ids': ids, 'limit': limit, 'lo': lo, 'hi': hi, 'out': out}
+        return g
 
     # ---- CUDA graphs ------------------------------------------------------------------------
     def bucket(self, n: int) -> int:
@@ -609,4 +653,5 @@ class Prefill:
 
     def release(self):
         self.graphs.clear()
+        self.batch_graphs.clear()
         self.pool = None

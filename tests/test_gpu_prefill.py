@@ -164,6 +164,34 @@ def test_batched_scoring_matches_single_requests():
         assert abs(float(pb[i].sum()) - 1.0) < 1e-4
 
 
+def test_batch_graph_replay_matches_eager_batch():
+    """A captured [B, L] batch graph replays each new batch (ids, limits and option slices
+    copied into its static buffers) with the eager batch's results, and its outputs are the
+    caller's own (a later replay does not overwrite them)."""
+    from mica_b200 import prefill as P
+    cfg = P.DecoderConfig(layers=3, vocab=4096)
+    model = P.random_decoder(cfg, torch.device('cuda'), seed=22)
+    pf = P.Prefill(model, torch.arange(0, 257), max_len=4096)
+    gen = torch.Generator().manual_seed(12)
+    batches = [[300, 511, 64, 1000], [1024, 700, 1, 999]]
+    ids = [[torch.randint(0, cfg.vocab, (n,), generator=gen).cuda() for n in lens] for lens in batches]
+    slices = [[(2, 2 + 10 * (i + 1)) for i in range(4)], [(0, 257), (5, 6), (2, 100), (2, 257)]]
+    with pytest.raises(ValueError):
+        pf.capture_batch(4, 1000)
+    pf.capture_batch(4, 1024)
+    got = [pf.score_batch(t, s) for t, s in zip(ids, slices)]
+    for (zg, pg), t, s in zip(got, ids, slices):
+        ze, pe = pf.score_batch(t, s, graphs=False)
+        assert torch.allclose(pg, pe, atol=1e-3, rtol=0)
+        assert torch.allclose(zg, ze, atol=2e-2, rtol=1e-2)
+        for i, (lo, hi) in enumerate(s):
+            assert abs(float(pg[i].sum()) - 1.0) < 1e-4
+            assert float(pg[i, :lo].abs().sum()) == 0.0 and float(pg[i, hi:].abs().sum()) == 0.0
+    assert not torch.equal(got[0][1], got[1][1])
+    pf.release()
+    assert not pf.batch_graphs
+
+
 # ---------------------------------------------------------------------------------------
 # A model read from an int8-w8a8/1 weights folder written by the reference's convert with
 # activation statistics: per-projection smoothing (split q/k/v and gate/up paths), down and
