@@ -74,6 +74,7 @@ extern "C" {
 #define MICA_DEV_TIMEOUT_GRID       4
 #define MICA_DEV_TIMEOUT_DRAIN      5
 #define MICA_DEV_TIMEOUT_SELFTEST   6
+#define MICA_DEV_TIMEOUT_STREAMK    7   /* a stream-K CTA waited too long for its neighbour's partial */
 
 typedef struct mica_caps {
     int device;             /* CUDA ordinal queried                                     */
@@ -85,7 +86,7 @@ typedef struct mica_caps {
     int pair_clusters;      /* co-resident CTA pairs for the 256-row GEMM tiles         */
 } mica_caps;
 
-#define MICA_ABI_VERSION 3
+#define MICA_ABI_VERSION 4
 
 /* Capability query. Replaces int8_kernels.available() (v0.5/serving/lib/int8_kernels.py:146-159)
  * and the capability probe in _device_cc (:130-143). Fills *caps for `device`.         */
@@ -152,12 +153,37 @@ int mica_w8a8_gemm(const int8_t* A, long lda, const int8_t* B, long ldb,
  *   splits   K split of each 128-row tile across a cluster of that many CTAs, reduced in
  *           distributed shared memory (exact): 0 = library choice (split only when fewer
  *           than half the SMs would get a tile), 1 = never, 2..8 = forced (MICA_ERR_UNSUPPORTED
- *           when a rank would get no k-block). Ignored with max_ctas > 0; not with block_m 256. */
+ *           when a rank would get no k-block). Ignored with max_ctas > 0; not with block_m 256.
+ *           MICA_SPLIT_STREAM_K asks for the stream-K kernel, which needs a workspace: use
+ *           mica_w8a8_gemm_ex (here it returns MICA_ERR_WORKSPACE).                          */
+#define MICA_SPLIT_STREAM_K (-1)
 int mica_w8a8_gemm_cfg(const int8_t* A, long lda, const int8_t* B, long ldb,
                        const float* sa, const float* sb, const float* bias,
                        void* C, int c_dtype, long ldc,
                        int M, int N, int K, int block_m, int block_n, int max_ctas, int splits,
                        void* stream);
+
+/* As mica_w8a8_gemm_cfg with a device workspace, which lets the library run a grid whose
+ * last wave would leave most SMs idle as stream-K: one CTA per SM, every CTA the same number
+ * of (tile, k-block) units, a tile cut between two CTAs finished by the one that reaches it
+ * last from the other's int32 partial (exact: the same int32 sums as the data-parallel
+ * kernel). Used by the library choice (splits 0, block_m 128 or 0, max_ctas 0) when it
+ * shortens the critical path, and by splits = MICA_SPLIT_STREAM_K (block_n 128 or 256).
+ * workspace: mica_w8a8_gemm_workspace_bytes(...) bytes for the same arguments, 16-byte
+ * aligned, reserved for this call until it completes on `stream` (the call clears what it
+ * needs). With splits 0 and a NULL or smaller workspace the data-parallel kernel runs.
+ * Config 0 of the reference's benchmarks (M 512, N 9728, K 2560: 152 tiles of 128 x 256 on
+ * 148 SMs) is the case it is for. No counterpart in the reference (its Triton mm_i8 grid is
+ * one program per tile, v0.5/serving/kernel_src/kernels.py:41-69).                       */
+int mica_w8a8_gemm_ex(const int8_t* A, long lda, const int8_t* B, long ldb,
+                      const float* sa, const float* sb, const float* bias,
+                      void* C, int c_dtype, long ldc,
+                      int M, int N, int K, int block_m, int block_n, int max_ctas, int splits,
+                      void* workspace, size_t workspace_bytes, void* stream);
+
+/* Workspace bytes mica_w8a8_gemm_ex uses with these arguments on the current device
+ * (0: none; also 0 for arguments it would reject).                                      */
+size_t mica_w8a8_gemm_workspace_bytes(int M, int N, int K, int block_m, int block_n, int max_ctas, int splits);
 
 /* Fused MLP front half: gate_up W8A8 GEMM + SwiGLU + next-layer per-token quantisation.
  *   Bgu [2*I, K]: gate and up weight rows interleaved in groups of 16

@@ -39,7 +39,9 @@ DEV_ERRORS = {
     4: 'timeout_grid',
     5: 'timeout_drain',
     6: 'timeout_selftest',
+    7: 'timeout_streamk',
 }
+SPLIT_STREAM_K = -1
 
 # name -> (restype, argtypes); mirrors include/mica_w8a8.h
 _P, _I, _L, _F, _Z = ctypes.c_void_p, ctypes.c_int, ctypes.c_long, ctypes.c_float, ctypes.c_size_t
@@ -70,6 +72,8 @@ SIGNATURES = {
     ),
     'mica_w8a8_gemm': (_I, [_P, _L, _P, _L, _P, _P, _P, _P, _I, _L, _I, _I, _I, _P]),
     'mica_w8a8_gemm_cfg': (_I, [_P, _L, _P, _L, _P, _P, _P, _P, _I, _L, _I, _I, _I, _I, _I, _I, _I, _P]),
+    'mica_w8a8_gemm_ex': (_I, [_P, _L, _P, _L, _P, _P, _P, _P, _I, _L, _I, _I, _I, _I, _I, _I, _I, _P, _Z, _P]),
+    'mica_w8a8_gemm_workspace_bytes': (_Z, [_I, _I, _I, _I, _I, _I, _I]),
     'mica_swiglu_workspace_bytes': (_Z, [_I]),
     'mica_w8a8_gemm_swiglu_quant': (
         _I,

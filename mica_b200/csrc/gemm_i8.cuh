@@ -82,6 +82,44 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t
                  : "memory");
 }
 
+// One 32-column chunk of the dequant epilogue for this lane's row: y = (acc * sa) * sb (+ bias)
+// in fp32, no FMA, cast to OutT and written to chunk `cc` of the lane's 128-byte row of a
+// 128-byte-swizzled store box. Lane j of the warp holds sb / bias of column j of the chunk.
+template <typename OutT>
+__device__ __forceinline__ void dequant_chunk_to_box(const uint32_t (&r)[32], float sa_v, float sb_l, float bias_l,
+                                                     bool has_bias, uint32_t box_row, int cc) {
+    const int lane = threadIdx.x & 31;
+    float y[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+        const float sbj = __shfl_sync(0xffffffffu, sb_l, j);
+        y[j] = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[j])), sa_v), sbj);
+    }
+    if (has_bias) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) y[j] = __fadd_rn(y[j], __shfl_sync(0xffffffffu, bias_l, j));
+    }
+    if constexpr (sizeof(OutT) == 2) {
+        uint32_t p[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            if constexpr (std::is_same<OutT, __half>::value) p[j] = pack_f16(y[2 * j], y[2 * j + 1]);
+            else p[j] = pack_bf16(y[2 * j], y[2 * j + 1]);
+        }
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const int chunk = cc * 4 + c;
+            st_shared_v4(box_row + ((chunk ^ (lane & 7)) << 4), p[4 * c], p[4 * c + 1], p[4 * c + 2], p[4 * c + 3]);
+        }
+    } else {
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+            st_shared_v4(box_row + ((c ^ (lane & 7)) << 4), __float_as_uint(y[4 * c]), __float_as_uint(y[4 * c + 1]),
+                         __float_as_uint(y[4 * c + 2]), __float_as_uint(y[4 * c + 3]));
+        }
+    }
+}
+
 // f[e] = RN(f[e] * inv[e]) for eight consecutive columns (inv 16-byte aligned).
 __device__ __forceinline__ void scale8(float (&f)[8], const float* inv) {
     const float4 a = __ldg(reinterpret_cast<const float4*>(inv));
@@ -304,37 +342,7 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
                         uint32_t r[32];
                         tmem_ld_32x32b_x32(t_row + col0, r);
                         tmem_ld_wait();
-                        float y[32];
-#pragma unroll
-                        for (int j = 0; j < 32; ++j) {
-                            const float sbj = __shfl_sync(0xffffffffu, sb_l, j);
-                            y[j] = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[j])), sa_v), sbj);
-                        }
-                        if (args.bias != nullptr) {
-#pragma unroll
-                            for (int j = 0; j < 32; ++j) y[j] = __fadd_rn(y[j], __shfl_sync(0xffffffffu, bias_l, j));
-                        }
-                        if constexpr (sizeof(OutT) == 2) {
-                            uint32_t p[16];
-#pragma unroll
-                            for (int j = 0; j < 16; ++j) {
-                                if constexpr (std::is_same<OutT, __half>::value) p[j] = pack_f16(y[2 * j], y[2 * j + 1]);
-                                else p[j] = pack_bf16(y[2 * j], y[2 * j + 1]);
-                            }
-#pragma unroll
-                            for (int c = 0; c < 4; ++c) {
-                                const int chunk = cc * 4 + c;
-                                st_shared_v4(box_row + ((chunk ^ (lane & 7)) << 4), p[4 * c], p[4 * c + 1],
-                                             p[4 * c + 2], p[4 * c + 3]);
-                            }
-                        } else {
-#pragma unroll
-                            for (int c = 0; c < 8; ++c) {
-                                st_shared_v4(box_row + ((c ^ (lane & 7)) << 4), __float_as_uint(y[4 * c]),
-                                             __float_as_uint(y[4 * c + 1]), __float_as_uint(y[4 * c + 2]),
-                                             __float_as_uint(y[4 * c + 3]));
-                            }
-                        }
+                        dequant_chunk_to_box<OutT>(r, sa_v, sb_l, bias_l, args.bias != nullptr, box_row, cc);
                     }
                     if (bx + PARTS >= BOXES) {
                         // this warp's last read of the accumulator: hand it back to the MMA warp

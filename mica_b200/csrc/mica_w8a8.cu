@@ -17,6 +17,7 @@
 #include "gemm_i8.cuh"
 #include "gemm_i8_pair.cuh"
 #include "gemm_i8_splitk.cuh"
+#include "gemm_i8_streamk.cuh"
 #include "quant.cuh"
 #include "readout.cuh"
 #include "qk_rope.cuh"
@@ -313,6 +314,124 @@ static void pick_tile(int M, int N, int sms, int* bm, int* bn) {
     *bn = t256 >= sms ? 256 : (2 * t128 >= sms ? 128 : 64);
 }
 
+// ---- stream-K kernels ---------------------------------------------------------------------
+// The library choice uses stream-K only for a grid of one to two waves whose second wave is
+// long and mostly empty. On B200 the exchange of a cut tile costs about 6 us at the end of the
+// kernel (the finishing CTA of a short last segment waits for its neighbour's partial), the
+// flag clear about 2 us, and a run of many waves loses the round-robin order's L2 reuse, so
+// the data-parallel kernel wins unless the critical path drops by SK_MIN_GAIN_KB k-blocks or
+// more (measured: M 2048, N 2560, K 9728 at 128 x 256 goes from 69.6 to 57.4 us; M 512, N 9728,
+// K 2560 rises from 28.7 to 32.9 us, and M 32768, N 2560, K 9728 from 582 to 713 us).
+constexpr long SK_MIN_GAIN_KB = 40;
+
+static bool want_streamk(long tiles, int num_kb, int sms) {
+    if (tiles < sms || tiles >= 2L * sms || sms > 256) return false;
+    const long dp = 2L * num_kb;
+    const long sk = (tiles * num_kb + sms - 1) / sms;
+    return dp - sk >= SK_MIN_GAIN_KB;
+}
+
+static size_t streamk_ws_bytes(int ctas, int bn) {
+    return static_cast<size_t>(SK_FLAG_BYTES) + static_cast<size_t>(ctas) * 128u * static_cast<size_t>(bn) * 4u;
+}
+
+template <int BN, typename OutT>
+static int streamk_prepare() {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    static std::atomic<uint64_t> done{0};
+    const uint64_t bit = 1ull << (dev & 63);
+    if (done.load(std::memory_order_acquire) & bit) return MICA_OK;
+    cudaError_t e = cudaFuncSetAttribute(gemm_i8_streamk_kernel<BN, OutT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         GemmShape<BN, 4>::SMEM_BYTES);
+    if (e != cudaSuccess) { set_cuda_error(e); return MICA_ERR_CUDA; }
+    done.fetch_or(bit, std::memory_order_release);
+    return MICA_OK;
+}
+
+template <int BN, typename OutT>
+static int streamk_launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const GemmArgs& args,
+                          int ctas, void* workspace, cudaStream_t stream) {
+    int rc = streamk_prepare<BN, OutT>();
+    if (rc) return rc;
+    cudaError_t e = cudaMemsetAsync(workspace, 0, SK_FLAG_BYTES, stream);
+    if (e != cudaSuccess) { set_cuda_error(e); return MICA_ERR_CUDA; }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(ctas));
+    cfg.blockDim = dim3(GemmShape<BN, 4>::THREADS);
+    cfg.dynamicSmemBytes = GemmShape<BN, 4>::SMEM_BYTES;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;     // every CTA resident: a FINISH waits on its neighbour
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, gemm_i8_streamk_kernel<BN, OutT>, ta, tb, tc, args,
+                           static_cast<uint8_t*>(workspace));
+    if (e != cudaSuccess) { set_cuda_error(e); return MICA_ERR_CUDA; }
+    return launch_status();
+}
+
+template <int BN>
+static int streamk_dispatch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const GemmArgs& g,
+                            int c_dtype, int ctas, void* ws, cudaStream_t st) {
+    if (c_dtype == MICA_DT_BF16) return streamk_launch<BN, __nv_bfloat16>(ta, tb, tc, g, ctas, ws, st);
+    if (c_dtype == MICA_DT_FP16) return streamk_launch<BN, __half>(ta, tb, tc, g, ctas, ws, st);
+    return streamk_launch<BN, float>(ta, tb, tc, g, ctas, ws, st);
+}
+
+// The GEMM's launch plan from its arguments (shared by the call and the workspace query).
+struct GemmPlan {
+    int bm, bn;
+    bool streamk;
+    int sk_ctas;
+    size_t ws_bytes;
+};
+
+static int gemm_tile_args_ok(int block_m, int block_n, int max_ctas, int splits) {
+    if (block_m != 0 && block_m != 128 && block_m != 256) return MICA_ERR_ARG;
+    if (block_n != 0 && block_n != 64 && block_n != 128 && block_n != 256) return MICA_ERR_ARG;
+    if (block_m == 256 && block_n == 64) return MICA_ERR_ARG;
+    if (max_ctas < 0 || splits < MICA_SPLIT_STREAM_K || splits > 8 || (splits > 1 && block_m == 256) ||
+        (splits == MICA_SPLIT_STREAM_K && (block_m == 256 || max_ctas > 0)))
+        return MICA_ERR_ARG;
+    return MICA_OK;
+}
+
+static int gemm_plan(int M, int N, int K, int block_m, int block_n, int max_ctas, int splits, int sms,
+                     GemmPlan* p) {
+    if (int rc = gemm_tile_args_ok(block_m, block_n, max_ctas, splits)) return rc;
+    int bm = block_m, bn = block_n;
+    if (bm == 0 && bn == 0) {
+        pick_tile(M, N, sms, &bm, &bn);
+    } else if (bm == 0) {
+        bm = 128;
+    } else if (bn == 0) {
+        int pm = 0;
+        pick_tile(M, N, sms, &pm, &bn);
+        if (bm == 256 && bn == 64) bn = 128;
+    }
+    p->bm = bm;
+    p->bn = bn;
+    p->streamk = false;
+    p->sk_ctas = 0;
+    p->ws_bytes = 0;
+    if (bm != 128 || max_ctas > 0) return MICA_OK;
+    const long tiles = static_cast<long>((M + 127) / 128) * ((N + bn - 1) / bn);
+    const int num_kb = (K + 127) / 128;
+    if (splits == MICA_SPLIT_STREAM_K) {
+        if (bn == 64 || sms > 256) return MICA_ERR_UNSUPPORTED;
+        p->streamk = true;
+    } else if (splits == 0 && bn != 64 && want_streamk(tiles, num_kb, sms)) {
+        p->streamk = true;
+    }
+    if (p->streamk) {
+        p->sk_ctas = static_cast<int>(tiles < sms ? tiles : sms);
+        p->ws_bytes = streamk_ws_bytes(p->sk_ctas, bn);
+    }
+    return MICA_OK;
+}
+
 }  // namespace mica_host
 
 using namespace mica_host;
@@ -391,6 +510,16 @@ int mica_preload(int* n_kernels) {
         (rc = splitk_prepare_all<256>(dev)))
         return rc;
     n += 9;
+#define PREP_SK(BN, T)                                           \
+    if ((rc = streamk_prepare<BN, T>()) != MICA_OK) return rc; \
+    ++n;
+    PREP_SK(128, __nv_bfloat16)
+    PREP_SK(256, __nv_bfloat16)
+    PREP_SK(128, __half)
+    PREP_SK(256, __half)
+    PREP_SK(128, float)
+    PREP_SK(256, float)
+#undef PREP_SK
     if (n_kernels) *n_kernels = n;
     return MICA_OK;
 }
@@ -531,28 +660,43 @@ static int gemm_dispatch_out(const CUtensorMap& ta, const CUtensorMap& tb, const
     return gemm_launch<BN, EPI_DEQUANT, float>(ta, tb, tc, g, grid, false, st);
 }
 
+size_t mica_w8a8_gemm_workspace_bytes(int M, int N, int K, int block_m, int block_n, int max_ctas, int splits) {
+    if (M <= 0 || N <= 0 || K <= 0) return 0;
+    int sms = 0;
+    if (check_device(&sms)) return 0;
+    GemmPlan p;
+    if (gemm_plan(M, N, K, block_m, block_n, max_ctas, splits, sms, &p)) return 0;
+    return p.ws_bytes;
+}
+
 int mica_w8a8_gemm_cfg(const int8_t* A, long lda, const int8_t* B, long ldb, const float* sa, const float* sb,
                        const float* bias, void* C, int c_dtype, long ldc, int M, int N, int K, int block_m,
                        int block_n, int max_ctas, int splits, void* stream) {
+    return mica_w8a8_gemm_ex(A, lda, B, ldb, sa, sb, bias, C, c_dtype, ldc, M, N, K, block_m, block_n, max_ctas,
+                             splits, nullptr, 0, stream);
+}
+
+int mica_w8a8_gemm_ex(const int8_t* A, long lda, const int8_t* B, long ldb, const float* sa, const float* sb,
+                      const float* bias, void* C, int c_dtype, long ldc, int M, int N, int K, int block_m,
+                      int block_n, int max_ctas, int splits, void* workspace, size_t workspace_bytes,
+                      void* stream) {
     int rc = gemm_checks(A, lda, B, ldb, sa, sb, bias, C, c_dtype, ldc, M, N, K);
     if (rc) return rc;
-    if (block_m != 0 && block_m != 128 && block_m != 256) return MICA_ERR_ARG;
-    if (block_n != 0 && block_n != 64 && block_n != 128 && block_n != 256) return MICA_ERR_ARG;
-    if (block_m == 256 && block_n == 64) return MICA_ERR_ARG;
-    if (max_ctas < 0 || splits < 0 || splits > 8 || (splits > 1 && block_m == 256)) return MICA_ERR_ARG;
+    if ((rc = gemm_tile_args_ok(block_m, block_n, max_ctas, splits))) return rc;
+    if (workspace && !aligned16(workspace)) return MICA_ERR_ALIGN;
     int sms = 0;
     if ((rc = check_device(&sms))) return rc;
-    if (M == 0) return MICA_OK;
-    int bm = block_m, bn = block_n;
-    if (bm == 0 && bn == 0) {
-        pick_tile(M, N, sms, &bm, &bn);
-    } else if (bm == 0) {
-        bm = 128;
-    } else if (bn == 0) {
-        int pm = 0;
-        pick_tile(M, N, sms, &pm, &bn);
-        if (bm == 256 && bn == 64) bn = 128;
+    GemmPlan plan;
+    if ((rc = gemm_plan(M, N, K, block_m, block_n, max_ctas, splits, sms, &plan))) return rc;
+    if (plan.streamk) {
+        const bool forced = splits == MICA_SPLIT_STREAM_K;
+        if (!workspace || workspace_bytes < plan.ws_bytes) {
+            if (forced) return MICA_ERR_WORKSPACE;
+            plan.streamk = false;                 // library choice without room for it: data-parallel
+        }
     }
+    if (M == 0) return MICA_OK;
+    const int bm = plan.bm, bn = plan.bn;
     CUtensorMap ta, tb, tc;
     const CUtensorMapDataType cdt = c_dtype == MICA_DT_BF16   ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                     : c_dtype == MICA_DT_FP16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
@@ -577,6 +721,10 @@ int mica_w8a8_gemm_cfg(const int8_t* A, long lda, const int8_t* B, long ldb, con
         if (c_dtype == MICA_DT_BF16) return pair_launch<128, __nv_bfloat16>(ta, tb, tc, g, tiles, max_ctas, st);
         if (c_dtype == MICA_DT_FP16) return pair_launch<128, __half>(ta, tb, tc, g, tiles, max_ctas, st);
         return pair_launch<128, float>(ta, tb, tc, g, tiles, max_ctas, st);
+    }
+    if (plan.streamk) {
+        if (bn == 256) return streamk_dispatch<256>(ta, tb, tc, g, c_dtype, plan.sk_ctas, workspace, st);
+        return streamk_dispatch<128>(ta, tb, tc, g, c_dtype, plan.sk_ctas, workspace, st);
     }
     const long tiles = static_cast<long>((M + 127) / 128) * ((N + bn - 1) / bn);
     if (splits != 1 && max_ctas == 0) {

@@ -106,20 +106,39 @@ def _(x, residual, gamma, inv, eps, style, round_mode, want_y, want_q):
 def w8a8_gemm(qx: torch.Tensor, sx: torch.Tensor, qw: torch.Tensor, sw: torch.Tensor, bias: Optional[torch.Tensor],
               out_dtype: int, tile: int) -> torch.Tensor:
     """tile = splits * 10**6 + block_m * 1000 + block_n (e.g. 256256 = CTA pair, 256 x 256;
-    1128064 = 128 x 64 never split; 4128256 = 128 x 256 split four ways), 0 = library choice."""
+    1128064 = 128 x 64 never split; 4128256 = 128 x 256 split four ways; 9128256 = 128 x 256
+    stream-K), 0 = library choice."""
     m, k = qx.shape
     n = qw.shape[0]
     out = torch.empty((m, n), dtype=OUT_DTYPES[out_dtype], device=qx.device)
-    with _on(qx):
-        N.call('mica_w8a8_gemm_cfg', qx.data_ptr(), qx.stride(0), qw.data_ptr(), qw.stride(0), sx.data_ptr(),
-               sw.data_ptr(), _ptr(bias), out.data_ptr(), out_dtype, out.stride(0), m, n, k, *_tile_args(tile),
-               _stream(qx))
+    _gemm(qx, sx, qw, sw, bias, out, out_dtype, tile)
     return out
 
 
 def _tile_args(tile: int):
-    """(block_m, block_n, max_ctas, splits) of a tile code."""
-    return (tile // 1000) % 1000, tile % 1000, 0, tile // 1000000
+    """(block_m, block_n, max_ctas, splits) of a tile code (splits digit 9 = stream-K)."""
+    splits = tile // 1000000
+    return (tile // 1000) % 1000, tile % 1000, 0, N.SPLIT_STREAM_K if splits == 9 else splits
+
+
+_WS_BYTES = {}
+
+
+def _gemm(qx, sx, qw, sw, bias, out, out_code, tile):
+    """One mica_w8a8_gemm_ex call; the stream-K workspace, when the plan uses one, comes from
+    torch's allocator on the current stream (reserved until the kernel is done with it)."""
+    m, k = qx.shape
+    n = qw.shape[0]
+    args = _tile_args(tile)
+    with _on(qx):
+        key = (qx.device.index, m, n, k, tile)
+        need = _WS_BYTES.get(key)
+        if need is None:
+            need = _WS_BYTES[key] = int(N.lib().mica_w8a8_gemm_workspace_bytes(m, n, k, *args))
+        ws = torch.empty((need,), dtype=torch.uint8, device=qx.device) if need else None
+        N.call('mica_w8a8_gemm_ex', qx.data_ptr(), qx.stride(0), qw.data_ptr(), qw.stride(0), sx.data_ptr(),
+               sw.data_ptr(), _ptr(bias), out.data_ptr(), out_code, out.stride(0), m, n, k, *args,
+               _ptr(ws), need, _stream(qx))
 
 
 @w8a8_gemm.register_fake
@@ -136,12 +155,7 @@ def w8a8_gemm_into(qx: torch.Tensor, sx: torch.Tensor, qw: torch.Tensor, sw: tor
     """As w8a8_gemm, writing into `out` [M, N] (unit column stride, any row stride): e.g. the
     q, k and v slices of one qkv buffer when the three projections quantise their input
     differently."""
-    m, k = qx.shape
-    n = qw.shape[0]
-    with _on(qx):
-        N.call('mica_w8a8_gemm_cfg', qx.data_ptr(), qx.stride(0), qw.data_ptr(), qw.stride(0), sx.data_ptr(),
-               sw.data_ptr(), _ptr(bias), out.data_ptr(), _OUT_CODE[out.dtype], out.stride(0), m, n, k,
-               *_tile_args(tile), _stream(qx))
+    _gemm(qx, sx, qw, sw, bias, out, _OUT_CODE[out.dtype], tile)
 
 
 @w8a8_gemm_into.register_fake

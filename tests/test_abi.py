@@ -62,6 +62,14 @@ def test_entry_points_reject_bad_arguments_without_touching_a_gpu(lib_path):
     assert lib.mica_w8a8_gemm_cfg(16, 32, 16, 32, 16, 16, None, 16, 0, 8, 4, 8, 32, 256, 64, 0, 0, None) == 1
     assert lib.mica_w8a8_gemm_cfg(16, 32, 16, 32, 16, 16, None, 16, 0, 8, 4, 8, 32, 128, 64, 0, 9, None) == 1  # splits
     assert lib.mica_w8a8_gemm_cfg(16, 32, 16, 32, 16, 16, None, 16, 0, 8, 4, 8, 32, 256, 256, 0, 2, None) == 1
+    # stream-K: not on CTA pairs, not with a capped grid, splits below -1 rejected; workspace alignment
+    sk = N.SPLIT_STREAM_K
+    assert lib.mica_w8a8_gemm_ex(16, 32, 16, 32, 16, 16, None, 16, 0, 8, 4, 8, 32, 256, 256, 0, sk, None, 0, None) == 1
+    assert lib.mica_w8a8_gemm_ex(16, 32, 16, 32, 16, 16, None, 16, 0, 8, 4, 8, 32, 128, 256, 4, sk, None, 0, None) == 1
+    assert lib.mica_w8a8_gemm_ex(16, 32, 16, 32, 16, 16, None, 16, 0, 8, 4, 8, 32, 128, 256, 0, -2, None, 0, None) == 1
+    assert lib.mica_w8a8_gemm_ex(16, 32, 16, 32, 16, 16, None, 16, 0, 8, 4, 8, 32, 128, 256, 0, sk, 24, 4096,
+                                 None) == 3
+    assert lib.mica_w8a8_gemm_workspace_bytes(512, 9728, 2560, 0, 0, 0, 0) == 0      # no device here
     assert lib.mica_w8a8_gemm_swiglu_quant(16, 32, 16, 32, 16, 16, None, None, 16, 32, 16, 32, 16, 4, 32, 32, 0,
                                            16, 8, None) == 7                                   # workspace
     assert lib.mica_option_logits(16, 0, 64, None, 0, 1e-6, 16, 0, 64, None, None, 16, 16, 1, None) == 2

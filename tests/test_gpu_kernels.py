@@ -423,3 +423,66 @@ def test_gemm_split_k_bit_exact(K, m, n, k, bn, splits):
     ref = O.dequant_out(acc, sx.numpy(), sw.numpy(), bias.numpy(), out='bf16')
     assert np.array_equal(to_np(yb.float()), ref)
     assert dev_error() == 0
+
+
+# ---------------------------------------------------------------------------------------
+# Stream-K (one CTA per SM, equal runs of (tile, k-block) units, a cut tile finished from its
+# neighbour's int32 partial): bit-exact against the oracle and the data-parallel kernel.
+@pytest.mark.parametrize('bn', [128, 256])
+@pytest.mark.parametrize('m,n,k', [(512, 9728, 2560), (2048, 2560, 4096), (1000, 9704, 2576), (77, 96, 1040),
+                                   (256, 19456, 2560)])
+def test_gemm_stream_k_bit_exact(K, m, n, k, bn):
+    g = torch.Generator().manual_seed(m + n + k + bn)
+    lo = 31 if k > 1024 else 127                    # |acc| < 2^24: the fp32 output is the exact int32
+    qx = torch.randint(-lo, lo + 1, (m, k), generator=g, dtype=torch.int8)
+    qw = torch.randint(-lo, lo + 1, (n, k), generator=g, dtype=torch.int8)
+    sk, dp = 9000000 + 128000 + bn, 1000000 + 128000 + bn
+    qxc, qwc = qx.cuda(), qw.cuda()
+    y = torch.ops.mica.w8a8_gemm(qxc, torch.ones(m).cuda(), qwc, torch.ones(n).cuda(), None, 2, sk)
+    acc = O.int_gemm_exact(qx.numpy(), qw.numpy())
+    assert np.array_equal(y.cpu().numpy().astype(np.int64), acc.astype(np.int64))
+    sx = (torch.rand(m, generator=g) * 0.05 + 1e-3).cuda()
+    sw = (torch.rand(n, generator=g) * 9e-3 + 1e-3).cuda()
+    bias = (torch.randn(n, generator=g) * 0.1).cuda()
+    yb = torch.ops.mica.w8a8_gemm(qxc, sx, qwc, sw, bias, 0, sk)
+    ref = O.dequant_out(acc, sx.cpu().numpy(), sw.cpu().numpy(), bias.cpu().numpy(), out='bf16')
+    assert np.array_equal(to_np(yb.float()), ref)
+    for code in (0, 1):
+        assert torch.equal(torch.ops.mica.w8a8_gemm(qxc, sx, qwc, sw, bias, code, sk),
+                           torch.ops.mica.w8a8_gemm(qxc, sx, qwc, sw, bias, code, dp))
+    assert dev_error() == 0
+
+
+def test_gemm_stream_k_library_choice(K):
+    """A grid of one to two waves with a long, mostly empty second wave (M 2048, N 2560,
+    K 9728: 160 tiles of 128 x 256 on 148 SMs, 76 k-blocks each) runs as stream-K by default,
+    with the data-parallel kernel's output; so does the strided-output form. Config 0's shape
+    (152 tiles of 20 k-blocks) and many-wave grids stay data-parallel. Without a workspace the
+    forced form is refused and the library choice runs data-parallel."""
+    from mica_b200 import _native as N
+    lib = N.lib()
+    assert lib.mica_w8a8_gemm_workspace_bytes(512, 9728, 2560, 0, 0, 0, 0) == 0
+    assert lib.mica_w8a8_gemm_workspace_bytes(32768, 2560, 9728, 0, 0, 0, 0) == 0
+    assert lib.mica_w8a8_gemm_workspace_bytes(512, 9728, 2560, 128, 256, 0, N.SPLIT_STREAM_K) > 0
+    m, n, k = 2048, 2560, 9728
+    assert lib.mica_w8a8_gemm_workspace_bytes(m, n, k, 0, 0, 0, 0) > 0
+    assert lib.mica_w8a8_gemm_workspace_bytes(m, n, k, 0, 0, 0, 1) == 0
+    g = torch.Generator(device='cuda').manual_seed(3)
+    qx = torch.randint(-127, 128, (m, k), generator=g, device='cuda', dtype=torch.int8)
+    qw = torch.randint(-127, 128, (n, k), generator=g, device='cuda', dtype=torch.int8)
+    sx = torch.rand(m, generator=g, device='cuda') * 0.05 + 1e-3
+    sw = torch.rand(n, generator=g, device='cuda') * 9e-3 + 1e-3
+    y0 = torch.ops.mica.w8a8_gemm(qx, sx, qw, sw, None, 0, 0)
+    y1 = torch.ops.mica.w8a8_gemm(qx, sx, qw, sw, None, 0, 1128256)
+    assert torch.equal(y0, y1)
+    out = torch.zeros((m, n + 64), dtype=torch.bfloat16, device='cuda')
+    torch.ops.mica.w8a8_gemm_into(qx, sx, qw, sw, None, out[:, 32:32 + n], 0)
+    assert torch.equal(out[:, 32:32 + n], y1) and not out[:, :32].any() and not out[:, 32 + n:].any()
+    y2 = torch.empty_like(y1)
+    stream = torch.cuda.current_stream().cuda_stream
+    args = (qx.data_ptr(), k, qw.data_ptr(), k, sx.data_ptr(), sw.data_ptr(), None, y2.data_ptr(), 0, n, m, n, k)
+    assert N.lib().mica_w8a8_gemm_cfg(*args, 128, 256, 0, N.SPLIT_STREAM_K, stream) == 7     # ERR_WORKSPACE
+    assert N.lib().mica_w8a8_gemm_ex(*args, 0, 0, 0, 0, None, 0, stream) == 0              # data-parallel
+    torch.cuda.synchronize()
+    assert torch.equal(y2, y1)
+    assert dev_error() == 0
