@@ -381,30 +381,65 @@ __device__ __forceinline__ void norm_row_warp(const QuantArgs& a, long row, int 
     ss = warp_sum(ss);
     const float rs = __frsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(a.K)), a.eps));
     float am = 0.f;
+    if (a.norm_style == MICA_NORM_WEIGHT && inv == nullptr) {
+        // y = T(w * T(x * rs)) on packed pairs: the fp32 products x * rs go to T as one packed
+        // pair (cvt.rn), and w * h is a packed T multiply -- the single rounding of the exact
+        // product of two T values, which is what the fp32 multiply and cast give. The absmax
+        // runs on the packed pairs too (exact: the max is one of the values).
+        using T2 = typename std::conditional<std::is_same<T, __half>::value, __half2, __nv_bfloat162>::type;
+        uint32_t am2 = 0u;
 #pragma unroll
-    for (int i = 0; i < MAXV; ++i) {
-        const int idx = lane + 32 * i;
-        if (idx < nvec) {
-            float f[8], w[8];
-            unpack8<T>(v[i], f);
-            unpack8<T>(__ldg(reinterpret_cast<const uint4*>(gp + idx * 8)), w);
+        for (int i = 0; i < MAXV; ++i) {
+            const int idx = lane + 32 * i;
+            if (idx < nvec) {
+                float f[8];
+                unpack8<T>(v[i], f);
+                const uint4 wv = __ldg(reinterpret_cast<const uint4*>(gp + idx * 8));
+                const uint32_t ws[4] = {wv.x, wv.y, wv.z, wv.w};
+                uint32_t ys[4];
 #pragma unroll
-            for (int e = 0; e < 8; ++e) {
-                const float n = __fmul_rn(f[e], rs);
-                f[e] = a.norm_style == MICA_NORM_OFFSET ? round_to<T>(__fmul_rn(n, __fadd_rn(1.0f, w[e])))
-                                                        : round_to<T>(__fmul_rn(w[e], round_to<T>(n)));
+                for (int j = 0; j < 4; ++j) {
+                    T2 h;
+                    if constexpr (std::is_same<T, __half>::value)
+                        h = __floats2half2_rn(__fmul_rn(f[2 * j], rs), __fmul_rn(f[2 * j + 1], rs));
+                    else
+                        h = __floats2bfloat162_rn(__fmul_rn(f[2 * j], rs), __fmul_rn(f[2 * j + 1], rs));
+                    const T2 y = __hmul2(*reinterpret_cast<const T2*>(&ws[j]), h);
+                    ys[j] = *reinterpret_cast<const uint32_t*>(&y);
+                }
+                v[i] = make_uint4(ys[0], ys[1], ys[2], ys[3]);
+                if (y_row != nullptr) *reinterpret_cast<uint4*>(y_row + idx * 8) = v[i];
+                absmax8<T>(v[i], am2);
             }
-            v[i] = pack8<T>(f);
-            if (y_row != nullptr) *reinterpret_cast<uint4*>(y_row + idx * 8) = v[i];
-            if (inv != nullptr) {
-                const float4 i0 = __ldg(reinterpret_cast<const float4*>(inv + idx * 8));
-                const float4 i1 = __ldg(reinterpret_cast<const float4*>(inv + idx * 8) + 1);
-                const float iv[8] = {i0.x, i0.y, i0.z, i0.w, i1.x, i1.y, i1.z, i1.w};
+        }
+        const T2 m2 = *reinterpret_cast<const T2*>(&am2);
+        am = fmaxf(__low2float(m2), __high2float(m2));
+    } else {
 #pragma unroll
-                for (int e = 0; e < 8; ++e) f[e] = __fmul_rn(f[e], iv[e]);
+        for (int i = 0; i < MAXV; ++i) {
+            const int idx = lane + 32 * i;
+            if (idx < nvec) {
+                float f[8], w[8];
+                unpack8<T>(v[i], f);
+                unpack8<T>(__ldg(reinterpret_cast<const uint4*>(gp + idx * 8)), w);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    const float n = __fmul_rn(f[e], rs);
+                    f[e] = a.norm_style == MICA_NORM_OFFSET ? round_to<T>(__fmul_rn(n, __fadd_rn(1.0f, w[e])))
+                                                            : round_to<T>(__fmul_rn(w[e], round_to<T>(n)));
+                }
+                v[i] = pack8<T>(f);
+                if (y_row != nullptr) *reinterpret_cast<uint4*>(y_row + idx * 8) = v[i];
+                if (inv != nullptr) {
+                    const float4 i0 = __ldg(reinterpret_cast<const float4*>(inv + idx * 8));
+                    const float4 i1 = __ldg(reinterpret_cast<const float4*>(inv + idx * 8) + 1);
+                    const float iv[8] = {i0.x, i0.y, i0.z, i0.w, i1.x, i1.y, i1.z, i1.w};
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) f[e] = __fmul_rn(f[e], iv[e]);
+                }
+#pragma unroll
+                for (int e = 0; e < 8; ++e) am = fmaxf(am, fabsf(f[e]));
             }
-#pragma unroll
-            for (int e = 0; e < 8; ++e) am = fmaxf(am, fabsf(f[e]));
         }
     }
     if (a.q == nullptr) return;          // norm-only call
