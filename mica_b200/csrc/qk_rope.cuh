@@ -99,14 +99,23 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(const QkRopeArgs a) {
 // cos/sin of the token and both norm weights stay in registers across the token's H + KV
 // heads; each head costs a lane two 8-byte loads and stores, and one 4-step shuffle sequence
 // reduces both heads' sums of squares. Eight heads are loaded before any is rewritten (a store
-// could alias a later head's load, which would otherwise serialise them). Every step is fp32
-// arithmetic followed by an explicit bf16 rounding, the HF op sequence.
+// could alias a later head's load, which would otherwise serialise them).
+// Arithmetic follows the HF op sequence: the sum of squares and x * rsqrt(...) in fp32, the
+// cast to bf16 (one packed cvt.rn per pair), then bf16 ops on packed pairs -- w * h, q * cos,
+// rotate_half(q) * sin and their sum. A packed bf16 multiply is the single rounding of the
+// exact product, which is what the fp32 multiply and cast give; a packed add of two bf16
+// values equals the fp32 add and cast too (their fp32 sum is exact unless the exponents differ
+// by more than 15, and then the smaller term is far below half an ulp of the result either way).
+// The _rn forms keep the compiler from contracting a multiply and the add into one fma, which
+// would round once where the HF sequence rounds twice.
 __device__ __forceinline__ void unpack4_bf16(const uint2 w, float (&f)[4]) {
     f[0] = __uint_as_float(w.x << 16);
     f[1] = __uint_as_float(w.x & 0xFFFF0000u);
     f[2] = __uint_as_float(w.y << 16);
     f[3] = __uint_as_float(w.y & 0xFFFF0000u);
 }
+__device__ __forceinline__ __nv_bfloat162 bf2(uint32_t w) { return *reinterpret_cast<const __nv_bfloat162*>(&w); }
+__device__ __forceinline__ uint32_t bits2(__nv_bfloat162 v) { return *reinterpret_cast<const uint32_t*>(&v); }
 
 __global__ void __launch_bounds__(256) qk_norm_rope_token_kernel(const QkRopeArgs a) {
     constexpr int D = 128;
@@ -116,18 +125,22 @@ __global__ void __launch_bounds__(256) qk_norm_rope_token_kernel(const QkRopeArg
     const int half = lane >> 4;
     const int d = 4 * (lane & 15);
     const long p = a.pos ? a.pos[s] : a.pos0 + s;
-    float cl[4], ch[4], sl[4], sh[4], wql[4] = {}, wqh[4] = {}, wkl[4] = {}, wkh[4] = {};
-    unpack4_bf16(*reinterpret_cast<const uint2*>(a.cos + p * D + d), cl);
-    unpack4_bf16(*reinterpret_cast<const uint2*>(a.cos + p * D + D / 2 + d), ch);
-    unpack4_bf16(*reinterpret_cast<const uint2*>(a.sin + p * D + d), sl);
-    unpack4_bf16(*reinterpret_cast<const uint2*>(a.sin + p * D + D / 2 + d), sh);
+    // packed bf16 pairs: cos/sin of dims [d, d+4) (l) and [64+d, 64+d+4) (h); -sin for the
+    // rotated low half (rotate_half negates q's high half: (-y_h) * sin_l = y_h * (-sin_l))
+    const uint2 cl = *reinterpret_cast<const uint2*>(a.cos + p * D + d);
+    const uint2 ch = *reinterpret_cast<const uint2*>(a.cos + p * D + D / 2 + d);
+    const uint2 sl = *reinterpret_cast<const uint2*>(a.sin + p * D + d);
+    const uint2 sh = *reinterpret_cast<const uint2*>(a.sin + p * D + D / 2 + d);
+    const uint32_t cl2[2] = {cl.x, cl.y}, ch2[2] = {ch.x, ch.y}, sh2[2] = {sh.x, sh.y};
+    const uint32_t nsl2[2] = {sl.x ^ 0x80008000u, sl.y ^ 0x80008000u};
+    uint2 wql = make_uint2(0u, 0u), wqh = wql, wkl = wql, wkh = wql;
     if (a.H > 0) {
-        unpack4_bf16(*reinterpret_cast<const uint2*>(a.q_w + d), wql);
-        unpack4_bf16(*reinterpret_cast<const uint2*>(a.q_w + D / 2 + d), wqh);
+        wql = *reinterpret_cast<const uint2*>(a.q_w + d);
+        wqh = *reinterpret_cast<const uint2*>(a.q_w + D / 2 + d);
     }
     if (a.KV > 0) {
-        unpack4_bf16(*reinterpret_cast<const uint2*>(a.k_w + d), wkl);
-        unpack4_bf16(*reinterpret_cast<const uint2*>(a.k_w + D / 2 + d), wkh);
+        wkl = *reinterpret_cast<const uint2*>(a.k_w + d);
+        wkh = *reinterpret_cast<const uint2*>(a.k_w + D / 2 + d);
     }
     __nv_bfloat16* row = a.qkv + s * a.ld;
     const int heads = a.H + a.KV;
@@ -161,22 +174,21 @@ __global__ void __launch_bounds__(256) qk_norm_rope_token_kernel(const QkRopeArg
             if (h >= heads) continue;
             const float r = __frsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(D)), a.eps));
             const bool is_q = h < a.H;
-            float ol[4], oh[4];
+            const uint2 wl = is_q ? wql : wkl, wh = is_q ? wqh : wkh;
+            const uint32_t wl2[2] = {wl.x, wl.y}, wh2[2] = {wh.x, wh.y};
+            uint32_t ol[2], oh[2];
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const float wl = is_q ? wql[e] : wkl[e], wh = is_q ? wqh[e] : wkh[e];
-                const float yl = bf(__fmul_rn(wl, bf(__fmul_rn(fl[e], r))));
-                const float yh = bf(__fmul_rn(wh, bf(__fmul_rn(fh[e], r))));
-                ol[e] = __fadd_rn(bf(__fmul_rn(yl, cl[e])), bf(__fmul_rn(-yh, sl[e])));
-                oh[e] = __fadd_rn(bf(__fmul_rn(yh, ch[e])), bf(__fmul_rn(yl, sh[e])));
+            for (int k = 0; k < 2; ++k) {
+                const __nv_bfloat162 yl = __hmul2_rn(
+                    bf2(wl2[k]), __floats2bfloat162_rn(__fmul_rn(fl[2 * k], r), __fmul_rn(fl[2 * k + 1], r)));
+                const __nv_bfloat162 yh = __hmul2_rn(
+                    bf2(wh2[k]), __floats2bfloat162_rn(__fmul_rn(fh[2 * k], r), __fmul_rn(fh[2 * k + 1], r)));
+                ol[k] = bits2(__hadd2_rn(__hmul2_rn(yl, bf2(cl2[k])), __hmul2_rn(yh, bf2(nsl2[k]))));
+                oh[k] = bits2(__hadd2_rn(__hmul2_rn(yh, bf2(ch2[k])), __hmul2_rn(yl, bf2(sh2[k]))));
             }
             __nv_bfloat16* x = row + static_cast<long>(h) * D;
-            const __nv_bfloat162 l0 = __floats2bfloat162_rn(ol[0], ol[1]), l1 = __floats2bfloat162_rn(ol[2], ol[3]);
-            const __nv_bfloat162 g0 = __floats2bfloat162_rn(oh[0], oh[1]), g1 = __floats2bfloat162_rn(oh[2], oh[3]);
-            *reinterpret_cast<uint2*>(x + d) = make_uint2(*reinterpret_cast<const uint32_t*>(&l0),
-                                                          *reinterpret_cast<const uint32_t*>(&l1));
-            *reinterpret_cast<uint2*>(x + D / 2 + d) = make_uint2(*reinterpret_cast<const uint32_t*>(&g0),
-                                                                  *reinterpret_cast<const uint32_t*>(&g1));
+            *reinterpret_cast<uint2*>(x + d) = make_uint2(ol[0], ol[1]);
+            *reinterpret_cast<uint2*>(x + D / 2 + d) = make_uint2(oh[0], oh[1]);
         }
     }
 }

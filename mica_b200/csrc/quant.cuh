@@ -404,7 +404,7 @@ __device__ __forceinline__ void norm_row_warp(const QuantArgs& a, long row, int 
                         h = __floats2half2_rn(__fmul_rn(f[2 * j], rs), __fmul_rn(f[2 * j + 1], rs));
                     else
                         h = __floats2bfloat162_rn(__fmul_rn(f[2 * j], rs), __fmul_rn(f[2 * j + 1], rs));
-                    const T2 y = __hmul2(*reinterpret_cast<const T2*>(&ws[j]), h);
+                    const T2 y = __hmul2_rn(*reinterpret_cast<const T2*>(&ws[j]), h);
                     ys[j] = *reinterpret_cast<const uint32_t*>(&y);
                 }
                 v[i] = make_uint4(ys[0], ys[1], ys[2], ys[3]);

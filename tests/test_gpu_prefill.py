@@ -90,6 +90,35 @@ def test_full_dims_36_layers_scores_finite_and_deterministic():
     assert torch.equal(a, b)
 
 
+@pytest.mark.parametrize('S,H,KV', [(333, 32, 8), (64, 4, 2)])
+def test_qk_norm_rope_bit_exact_against_fixed_order_restatement(S, H, KV):
+    """The D = 128 kernel equals the oracle's restatement of the HF op sequence bit for bit
+    (the restatement fixes the sum of squares to the kernel's order): no step may be fused or
+    re-rounded. Rows scaled by 1e-3 and 50 and scattered positions included."""
+    from conftest import ORACLE as O
+    from mica_b200 import ops  # noqa: F401
+    from mica_b200 import prefill as P
+    D = 128
+    g = torch.Generator(device='cuda').manual_seed(S + 3 * H)
+    qkv = (torch.randn(S, (H + 2 * KV) * D, generator=g, device='cuda') * 3).to(torch.bfloat16)
+    qkv[:5] *= 1e-3
+    qkv[5:7] *= 50
+    qw = (1 + 0.1 * torch.randn(D, generator=g, device='cuda')).to(torch.bfloat16)
+    kw = (1 + 0.1 * torch.randn(D, generator=g, device='cuda')).to(torch.bfloat16)
+    cos, sin = P.rope_tables(P.DecoderConfig(head_dim=D), 8192, torch.device('cuda'))
+    pos = torch.randint(0, 8192, (S,), generator=g, device='cuda')
+    before = qkv.float().cpu().numpy()
+    torch.ops.mica.qk_norm_rope(qkv, qw, kw, cos, sin, pos, 0, H, KV, 1e-6)
+    after = qkv.float().cpu().numpy()
+    c = cos[pos].float().cpu().numpy()
+    sn = sin[pos].float().cpu().numpy()
+    for h in range(H + KV):
+        w = (qw if h < H else kw).float().cpu().numpy()
+        want = O.qk_norm_rope(before[:, h * D:(h + 1) * D], w, c, sn, 1e-6)
+        assert np.array_equal(after[:, h * D:(h + 1) * D], want), h
+    assert np.array_equal(after[:, (H + KV) * D:], before[:, (H + KV) * D:])
+
+
 def _hf_qk(x, w, cos, sin, eps):
     """HF Qwen3 q_norm/k_norm + apply_rotary_pos_emb as torch bf16 ops (the reference)."""
     xf = x.float()
