@@ -486,3 +486,30 @@ def test_gemm_stream_k_library_choice(K):
     torch.cuda.synchronize()
     assert torch.equal(y2, y1)
     assert dev_error() == 0
+
+
+def test_gemm_stream_k_in_a_cuda_graph(K):
+    """The stream-K plan (flag clear + cooperative launch, workspace from the graph's pool)
+    captures into a CUDA graph; replays on new inputs give the data-parallel kernel's output."""
+    m, n, k = 2048, 2560, 9728
+    g = torch.Generator(device='cuda').manual_seed(9)
+    qx = torch.randint(-127, 128, (m, k), generator=g, device='cuda', dtype=torch.int8)
+    qw = torch.randint(-127, 128, (n, k), generator=g, device='cuda', dtype=torch.int8)
+    sx = torch.rand(m, generator=g, device='cuda') * 0.05 + 1e-3
+    sw = torch.rand(n, generator=g, device='cuda') * 9e-3 + 1e-3
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        torch.ops.mica.w8a8_gemm(qx, sx, qw, sw, None, 0, 0)
+    torch.cuda.current_stream().wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        y = torch.ops.mica.w8a8_gemm(qx, sx, qw, sw, None, 0, 0)
+    for seed in (1, 2):
+        gg = torch.Generator(device='cuda').manual_seed(seed)
+        qx.copy_(torch.randint(-127, 128, (m, k), generator=gg, device='cuda', dtype=torch.int8))
+        graph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(y, torch.ops.mica.w8a8_gemm(qx, sx, qw, sw, None, 0, 1128256)), seed
+    del graph
+    assert dev_error() == 0
