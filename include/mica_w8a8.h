@@ -75,6 +75,7 @@ extern "C" {
 #define MICA_DEV_TIMEOUT_DRAIN      5
 #define MICA_DEV_TIMEOUT_SELFTEST   6
 #define MICA_DEV_TIMEOUT_STREAMK    7   /* a stream-K CTA waited too long for its neighbour's partial */
+#define MICA_DEV_BAD_LAUNCH         8   /* a kernel found its grid smaller than it needs and did nothing */
 
 typedef struct mica_caps {
     int device;             /* CUDA ordinal queried                                     */
@@ -148,7 +149,9 @@ int mica_w8a8_gemm(const int8_t* A, long lda, const int8_t* B, long ldb,
 /* As mica_w8a8_gemm with an explicit output tile, used by the tile tuner:
  *   block_m 128 = one CTA per tile; 256 = a pair of CTAs on two SMs sharing each MMA
  *           (tcgen05 cta_group::2), 0 = library choice;
- *   block_n 64 / 128 / 256 (pairs: 128 / 256), 0 = library choice;
+ *   block_n 64 / 128 / 256 (pairs: 128 / 256), 0 = library choice; 320 (single CTAs, splits
+ *           0 or 1) is for grids that fit one wave at that width (MICA_ERR_UNSUPPORTED otherwise):
+ *           the library picks it when 128 x 256 tiles would need between one and two waves;
  *   max_ctas caps the persistent grid (0 = all SMs / all co-resident pairs);
  *   splits   K split of each 128-row tile across a cluster of that many CTAs, reduced in
  *           distributed shared memory (exact): 0 = library choice (split only when fewer
@@ -172,9 +175,9 @@ int mica_w8a8_gemm_cfg(const int8_t* A, long lda, const int8_t* B, long ldb,
  * workspace: mica_w8a8_gemm_workspace_bytes(...) bytes for the same arguments, 16-byte
  * aligned, reserved for this call until it completes on `stream` (the call clears what it
  * needs). With splits 0 and a NULL or smaller workspace the data-parallel kernel runs.
- * Config 0 of the reference's benchmarks (M 512, N 9728, K 2560: 152 tiles of 128 x 256 on
- * 148 SMs) is the case it is for. No counterpart in the reference (its Triton mm_i8 grid is
- * one program per tile, v0.5/serving/kernel_src/kernels.py:41-69).                       */
+ * The library choice uses it where 128 x 320 tiles cannot fit the grid in one wave (e.g. M
+ * 2048, N 3072, K 9728). No counterpart in the reference (its Triton mm_i8 grid is one
+ * program per tile, v0.5/serving/kernel_src/kernels.py:41-69).                            */
 int mica_w8a8_gemm_ex(const int8_t* A, long lda, const int8_t* B, long ldb,
                       const float* sa, const float* sb, const float* bias,
                       void* C, int c_dtype, long ldc,

@@ -40,6 +40,7 @@ DEV_ERRORS = {
     5: 'timeout_drain',
     6: 'timeout_selftest',
     7: 'timeout_streamk',
+    8: 'bad_launch',
 }
 SPLIT_STREAM_K = -1
 

@@ -42,11 +42,18 @@ struct GemmShape {
     static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
     static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + AUX_BYTES;
     static constexpr int ACC_COLS = BN;                 // int32 accumulator columns per buffer
-    static constexpr int TMEM_COLS = (2 * BN < 32) ? 32 : 2 * BN;
+    // BN = 320 (wider than one MMA or one TMA box): two 160-wide halves per k-step, and one
+    // accumulator buffer only (2 x 320 columns exceed the 512 of tensor memory), so the host
+    // launches it with at most one tile per CTA.
+    static constexpr int HALVES = BN > 256 ? 2 : 1;
+    static constexpr int MMA_N = BN / HALVES;
+    static constexpr int ACC_BUFS = BN > 256 ? 1 : 2;
+    static constexpr int TMEM_COLS = ACC_BUFS * BN <= 32 ? 32 : (ACC_BUFS * BN <= 256 ? (ACC_BUFS * BN <= 128 ? 128 : 256) : 512);
     static constexpr int THREADS = 64 + 32 * EW;
     static_assert(EW == 4 || EW == 8, "epilogue warps");
     static_assert(STAGES >= 2, "not enough shared memory for a pipeline");
-    static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256, "BN");
+    static_assert(BN % 32 == 0 && BN >= 64 && (BN <= 256 || BN == 320), "BN");
+    static_assert(ACC_BUFS * BN <= TMEM_COLS && TMEM_COLS <= 512, "tensor memory");
     static_assert(SMEM_BYTES <= SMEM_OPTIN, "smem");
 };
 
@@ -200,6 +207,13 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
     const int num_n = (N + BN - 1) / BN;
     const int num_tiles = num_m * num_n;
     const int num_kb = (K + S::BK - 1) / S::BK;
+    if constexpr (S::ACC_BUFS == 1) {
+        // one accumulator buffer: every CTA may own one tile at most (the host sizes the grid)
+        if (static_cast<int>(gridDim.x) < num_tiles) {
+            if (threadIdx.x == 0) atomicExch(&g_dev_error, MICA_DEV_BAD_LAUNCH);
+            return;
+        }
+    }
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < STAGES; ++i) {
@@ -241,7 +255,10 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
                     }
                     mbar_arrive_expect_tx(&full_bar[st], S::STAGE_BYTES);
                     tma_load_2d(smem_a + st * S::A_BYTES, &tmap_a, &full_bar[st], kb * S::BK, m0);
-                    tma_load_2d_hint(smem_b + st * S::B_BYTES, &tmap_b, &full_bar[st], kb * S::BK, n0, pol_b);
+#pragma unroll
+                    for (int hf = 0; hf < S::HALVES; ++hf)
+                        tma_load_2d_hint(smem_b + st * S::B_BYTES + hf * S::MMA_N * S::BK, &tmap_b, &full_bar[st],
+                                         kb * S::BK, n0 + hf * S::MMA_N, pol_b);
                 }
             }
             // Drain: the last loads of each stage must land before this CTA's smem goes away.
@@ -253,7 +270,7 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
         __syncwarp();
     } else if (warp == 1) {
         // ------------------------------- MMA issuer ---------------------------------
-        constexpr uint32_t idesc = idesc_i8(S::BM, BN);
+        constexpr uint32_t idesc = idesc_i8(S::BM, S::MMA_N);
         const uint32_t a_base = smem_u32(smem_a);
         const uint32_t b_base = smem_u32(smem_b);
         uint32_t it = 0;
@@ -278,8 +295,11 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
                     const uint32_t b_addr = b_base + st * S::B_BYTES;
 #pragma unroll
                     for (int k = 0; k < S::BK / S::UMMA_K; ++k) {
-                        mma_i8(d_tmem, smem_desc_k128(a_addr + k * S::UMMA_K), smem_desc_k128(b_addr + k * S::UMMA_K),
-                               idesc, (kb | k) != 0 ? 1u : 0u);
+#pragma unroll
+                        for (int hf = 0; hf < S::HALVES; ++hf)
+                            mma_i8(d_tmem + hf * S::MMA_N, smem_desc_k128(a_addr + k * S::UMMA_K),
+                                   smem_desc_k128(b_addr + hf * S::MMA_N * S::BK + k * S::UMMA_K), idesc,
+                                   (kb | k) != 0 ? 1u : 0u);
                     }
                     mma_commit(&empty_bar[st]);          // frees the stage when these MMAs finish
                     if (kb == num_kb - 1) mma_commit(&tfull_bar[acc]);  // accumulator complete

@@ -310,8 +310,12 @@ static void pick_tile(int M, int N, int sms, int* bm, int* bn) {
     const long m_blocks = (M + 127) / 128;
     const long t256 = m_blocks * ((N + 255) / 256);
     const long t128 = m_blocks * ((N + 127) / 128);
+    const long t320 = m_blocks * ((N + 319) / 320);
     *bm = 128;
     *bn = t256 >= sms ? 256 : (2 * t128 >= sms ? 128 : 64);
+    // A grid of 128 x 256 tiles just past one wave (config 0: 152 tiles on 148 SMs) leaves its
+    // critical path at two tiles; 128 x 320 tiles fit one wave, each 1.25 tiles long.
+    if (t256 > sms && t256 < 2L * sms && t320 <= sms) *bn = 320;
 }
 
 // ---- stream-K kernels ---------------------------------------------------------------------
@@ -390,8 +394,9 @@ struct GemmPlan {
 
 static int gemm_tile_args_ok(int block_m, int block_n, int max_ctas, int splits) {
     if (block_m != 0 && block_m != 128 && block_m != 256) return MICA_ERR_ARG;
-    if (block_n != 0 && block_n != 64 && block_n != 128 && block_n != 256) return MICA_ERR_ARG;
-    if (block_m == 256 && block_n == 64) return MICA_ERR_ARG;
+    if (block_n != 0 && block_n != 64 && block_n != 128 && block_n != 256 && block_n != 320) return MICA_ERR_ARG;
+    if (block_m == 256 && (block_n == 64 || block_n == 320)) return MICA_ERR_ARG;
+    if (block_n == 320 && (splits > 1 || splits == MICA_SPLIT_STREAM_K)) return MICA_ERR_ARG;
     if (max_ctas < 0 || splits < MICA_SPLIT_STREAM_K || splits > 8 || (splits > 1 && block_m == 256) ||
         (splits == MICA_SPLIT_STREAM_K && (block_m == 256 || max_ctas > 0)))
         return MICA_ERR_ARG;
@@ -410,6 +415,7 @@ static int gemm_plan(int M, int N, int K, int block_m, int block_n, int max_ctas
         int pm = 0;
         pick_tile(M, N, sms, &pm, &bn);
         if (bm == 256 && bn == 64) bn = 128;
+        if (bm == 256 && bn == 320) bn = 256;
     }
     p->bm = bm;
     p->bn = bn;
@@ -422,7 +428,7 @@ static int gemm_plan(int M, int N, int K, int block_m, int block_n, int max_ctas
     if (splits == MICA_SPLIT_STREAM_K) {
         if (bn == 64 || sms > 256) return MICA_ERR_UNSUPPORTED;
         p->streamk = true;
-    } else if (splits == 0 && bn != 64 && want_streamk(tiles, num_kb, sms)) {
+    } else if (splits == 0 && (bn == 128 || bn == 256) && want_streamk(tiles, num_kb, sms)) {
         p->streamk = true;
     }
     if (p->streamk) {
@@ -489,6 +495,9 @@ int mica_preload(int* n_kernels) {
     PREP(64, EPI_DEQUANT, float)
     PREP(128, EPI_DEQUANT, float)
     PREP(256, EPI_DEQUANT, float)
+    PREP(320, EPI_DEQUANT, __nv_bfloat16)
+    PREP(320, EPI_DEQUANT, __half)
+    PREP(320, EPI_DEQUANT, float)
 #undef PREP
     if ((rc = gemm_prepare<128, EPI_SWIGLU, __nv_bfloat16, 8>()) != MICA_OK) return rc;
     if ((rc = gemm_prepare<256, EPI_SWIGLU, __nv_bfloat16, 8>()) != MICA_OK) return rc;
@@ -702,8 +711,9 @@ int mica_w8a8_gemm_ex(const int8_t* A, long lda, const int8_t* B, long ldb, cons
                                     : c_dtype == MICA_DT_FP16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
                                                               : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
     const uint32_t es = static_cast<uint32_t>(dt_size(c_dtype));
-    // A CTA of a pair loads 128 rows of A and bn/2 rows of B.
-    const uint32_t b_box = bm == 256 ? static_cast<uint32_t>(bn / 2) : static_cast<uint32_t>(bn);
+    // A CTA of a pair loads 128 rows of A and bn/2 rows of B; a 320-wide tile loads its B rows
+    // as two 160-row boxes.
+    const uint32_t b_box = (bm == 256 || bn == 320) ? static_cast<uint32_t>(bn / 2) : static_cast<uint32_t>(bn);
     if ((rc = make_tmap_2d(&ta, A, CU_TENSOR_MAP_DATA_TYPE_UINT8, K, M, lda, 128, 128)) ||
         (rc = make_tmap_2d(&tb, B, CU_TENSOR_MAP_DATA_TYPE_UINT8, K, N, ldb, 128, b_box)) ||
         (rc = make_tmap_2d(&tc, C, cdt, N, M, ldc * es, 128 / es, 32)))
@@ -727,6 +737,11 @@ int mica_w8a8_gemm_ex(const int8_t* A, long lda, const int8_t* B, long ldb, cons
         return streamk_dispatch<128>(ta, tb, tc, g, c_dtype, plan.sk_ctas, workspace, st);
     }
     const long tiles = static_cast<long>((M + 127) / 128) * ((N + bn - 1) / bn);
+    if (bn == 320) {
+        // one accumulator buffer per CTA: one tile per CTA, all in one wave
+        if (tiles > sms || (max_ctas > 0 && tiles > max_ctas)) return MICA_ERR_UNSUPPORTED;
+        return gemm_dispatch_out<320>(ta, tb, tc, g, c_dtype, static_cast<int>(tiles), st);
+    }
     if (splits != 1 && max_ctas == 0) {
         int dev = 0;
         cudaGetDevice(&dev);

@@ -62,6 +62,9 @@ def test_entry_points_reject_bad_arguments_without_touching_a_gpu(lib_path):
     assert lib.mica_w8a8_gemm_cfg(16, 32, 16, 32, 16, 16, None, 16, 0, 8, 4, 8, 32, 256, 64, 0, 0, None) == 1
     assert lib.mica_w8a8_gemm_cfg(16, 32, 16, 32, 16, 16, None, 16, 0, 8, 4, 8, 32, 128, 64, 0, 9, None) == 1  # splits
     assert lib.mica_w8a8_gemm_cfg(16, 32, 16, 32, 16, 16, None, 16, 0, 8, 4, 8, 32, 256, 256, 0, 2, None) == 1
+    # 128 x 320 tiles: single CTAs only, no K split
+    assert lib.mica_w8a8_gemm_cfg(16, 32, 16, 32, 16, 16, None, 16, 0, 8, 4, 8, 32, 256, 320, 0, 0, None) == 1
+    assert lib.mica_w8a8_gemm_cfg(16, 32, 16, 32, 16, 16, None, 16, 0, 8, 4, 8, 32, 128, 320, 0, 2, None) == 1
     # stream-K: not on CTA pairs, not with a capped grid, splits below -1 rejected; workspace alignment
     sk = N.SPLIT_STREAM_K
     assert lib.mica_w8a8_gemm_ex(16, 32, 16, 32, 16, 16, None, 16, 0, 8, 4, 8, 32, 256, 256, 0, sk, None, 0, None) == 1

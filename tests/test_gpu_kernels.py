@@ -454,17 +454,19 @@ def test_gemm_stream_k_bit_exact(K, m, n, k, bn):
 
 
 def test_gemm_stream_k_library_choice(K):
-    """A grid of one to two waves with a long, mostly empty second wave (M 2048, N 2560,
-    K 9728: 160 tiles of 128 x 256 on 148 SMs, 76 k-blocks each) runs as stream-K by default,
-    with the data-parallel kernel's output; so does the strided-output form. Config 0's shape
-    (152 tiles of 20 k-blocks) and many-wave grids stay data-parallel. Without a workspace the
-    forced form is refused and the library choice runs data-parallel."""
+    """A grid of one to two waves with a long, mostly empty second wave that 128 x 320 tiles
+    cannot fit in one wave (M 2048, N 3072, K 9728: 192 tiles of 128 x 256 on 148 SMs, 76
+    k-blocks each) runs as stream-K by default, with the data-parallel kernel's output; so does
+    the strided-output form. Grids that 128 x 320 tiles cover in one wave (config 0, M 2048 with
+    N 2560) and many-wave grids use no workspace. Without a workspace the forced form is refused
+    and the library choice runs data-parallel."""
     from mica_b200 import _native as N
     lib = N.lib()
     assert lib.mica_w8a8_gemm_workspace_bytes(512, 9728, 2560, 0, 0, 0, 0) == 0
+    assert lib.mica_w8a8_gemm_workspace_bytes(2048, 2560, 9728, 0, 0, 0, 0) == 0
     assert lib.mica_w8a8_gemm_workspace_bytes(32768, 2560, 9728, 0, 0, 0, 0) == 0
     assert lib.mica_w8a8_gemm_workspace_bytes(512, 9728, 2560, 128, 256, 0, N.SPLIT_STREAM_K) > 0
-    m, n, k = 2048, 2560, 9728
+    m, n, k = 2048, 3072, 9728
     assert lib.mica_w8a8_gemm_workspace_bytes(m, n, k, 0, 0, 0, 0) > 0
     assert lib.mica_w8a8_gemm_workspace_bytes(m, n, k, 0, 0, 0, 1) == 0
     g = torch.Generator(device='cuda').manual_seed(3)
@@ -491,7 +493,7 @@ def test_gemm_stream_k_library_choice(K):
 def test_gemm_stream_k_in_a_cuda_graph(K):
     """The stream-K plan (flag clear + cooperative launch, workspace from the graph's pool)
     captures into a CUDA graph; replays on new inputs give the data-parallel kernel's output."""
-    m, n, k = 2048, 2560, 9728
+    m, n, k = 2048, 3072, 9728
     g = torch.Generator(device='cuda').manual_seed(9)
     qx = torch.randint(-127, 128, (m, k), generator=g, device='cuda', dtype=torch.int8)
     qw = torch.randint(-127, 128, (n, k), generator=g, device='cuda', dtype=torch.int8)
@@ -512,4 +514,46 @@ def test_gemm_stream_k_in_a_cuda_graph(K):
         torch.cuda.synchronize()
         assert torch.equal(y, torch.ops.mica.w8a8_gemm(qx, sx, qw, sw, None, 0, 1128256)), seed
     del graph
+    assert dev_error() == 0
+
+
+# ---------------------------------------------------------------------------------------
+# 128 x 320 tiles (two 160-wide MMAs per k-step, one accumulator buffer, one tile per CTA):
+# the library's choice when 128 x 256 tiles just exceed one wave (config 0). Bit-exact.
+@pytest.mark.parametrize('m,n,k', [(512, 9728, 2560), (2048, 2560, 4096), (500, 9000, 2576), (77, 96, 1040),
+                                   (256, 19456, 2560)])
+def test_gemm_wide_tile_bit_exact(K, m, n, k):
+    g = torch.Generator().manual_seed(m + 2 * n + k)
+    lo = 31 if k > 1024 else 127                    # |acc| < 2^24: the fp32 output is the exact int32
+    qx = torch.randint(-lo, lo + 1, (m, k), generator=g, dtype=torch.int8)
+    qw = torch.randint(-lo, lo + 1, (n, k), generator=g, dtype=torch.int8)
+    qxc, qwc = qx.cuda(), qw.cuda()
+    y = torch.ops.mica.w8a8_gemm(qxc, torch.ones(m).cuda(), qwc, torch.ones(n).cuda(), None, 2, 128320)
+    acc = O.int_gemm_exact(qx.numpy(), qw.numpy())
+    assert np.array_equal(y.cpu().numpy().astype(np.int64), acc.astype(np.int64))
+    sx = (torch.rand(m, generator=g) * 0.05 + 1e-3).cuda()
+    sw = (torch.rand(n, generator=g) * 9e-3 + 1e-3).cuda()
+    bias = (torch.randn(n, generator=g) * 0.1).cuda()
+    yb = torch.ops.mica.w8a8_gemm(qxc, sx, qwc, sw, bias, 0, 128320)
+    ref = O.dequant_out(acc, sx.cpu().numpy(), sw.cpu().numpy(), bias.cpu().numpy(), out='bf16')
+    assert np.array_equal(to_np(yb.float()), ref)
+    for code in (0, 1):
+        assert torch.equal(torch.ops.mica.w8a8_gemm(qxc, sx, qwc, sw, bias, code, 128320),
+                           torch.ops.mica.w8a8_gemm(qxc, sx, qwc, sw, bias, code, 1128256))
+    assert torch.equal(torch.ops.mica.w8a8_gemm(qxc, sx, qwc, sw, bias, 0, 0), yb)   # library choice
+    assert dev_error() == 0
+
+
+def test_gemm_wide_tile_needs_one_wave(K):
+    """A forced 128 x 320 tile on a grid larger than one wave is refused before any launch."""
+    from mica_b200 import _native as N
+    m, n, k = 32768, 2560, 256
+    qx = torch.zeros((m, k), dtype=torch.int8, device='cuda')
+    qw = torch.zeros((n, k), dtype=torch.int8, device='cuda')
+    s = torch.ones(max(m, n), device='cuda')
+    y = torch.empty((m, n), dtype=torch.bfloat16, device='cuda')
+    st = torch.cuda.current_stream().cuda_stream
+    rc = N.lib().mica_w8a8_gemm_cfg(qx.data_ptr(), k, qw.data_ptr(), k, s.data_ptr(), s.data_ptr(), None,
+                                    y.data_ptr(), 0, n, m, n, k, 128, 320, 0, 0, st)
+    assert rc == 8                                   # MICA_ERR_UNSUPPORTED
     assert dev_error() == 0
