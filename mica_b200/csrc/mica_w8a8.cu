@@ -325,7 +325,10 @@ static void pick_tile(int M, int N, int sms, int* bm, int* bn) {
 // flag clear about 2 us, and a run of many waves loses the round-robin order's L2 reuse, so
 // the data-parallel kernel wins unless the critical path drops by SK_MIN_GAIN_KB k-blocks or
 // more (measured: M 2048, N 2560, K 9728 at 128 x 256 goes from 69.6 to 57.4 us; M 512, N 9728,
-// K 2560 rises from 28.7 to 32.9 us, and M 32768, N 2560, K 9728 from 582 to 713 us).
+// K 2560 rises from 28.7 to 32.9 us, and M 32768, N 2560, K 9728 from 582 to 713 us). It is
+// weighed only for 128- and 256-wide tiles: where pick_tile takes 128 x 320 tiles (the grid then
+// fits one wave) those win (55.3 us on the first shape above), so stream-K serves grids that
+// 128 x 320 tiles cannot fit in one wave (M 2048, N 3072, K 9728: 71.7 -> 65.6 us).
 constexpr long SK_MIN_GAIN_KB = 40;
 
 static bool want_streamk(long tiles, int num_kb, int sms) {
