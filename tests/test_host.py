@@ -156,3 +156,16 @@ def test_decoder_from_hf_state_quantises_like_reference_qlinear():
     assert np.array_equal(lay.gu_w[:16].numpy(), g_ref[:16]) and np.array_equal(lay.gu_w[32:48].numpy(), g_ref[16:32])
     cos, sin = P.rope_tables(cfg, 16, torch.device('cpu'))
     assert cos.shape == (16, 64) and cos.dtype == torch.bfloat16 and float(cos[0, 0]) == 1.0
+
+
+def test_tile_codes_decode_to_the_c_arguments():
+    """splits * 10**6 + block_m * 1000 + block_n; splits digit 9 asks for stream-K."""
+    from mica_b200 import _native as N
+    from mica_b200.ops import _tile_args
+    assert _tile_args(0) == (0, 0, 0, 0)
+    assert _tile_args(128256) == (128, 256, 0, 0)
+    assert _tile_args(128320) == (128, 320, 0, 0)
+    assert _tile_args(256256) == (256, 256, 0, 0)
+    assert _tile_args(1128064) == (128, 64, 0, 1)
+    assert _tile_args(4128256) == (128, 256, 0, 4)
+    assert _tile_args(9128256) == (128, 256, 0, N.SPLIT_STREAM_K)
