@@ -144,3 +144,14 @@ def test_a_rank_that_leaves_makes_its_peer_fail_not_hang(tmp_path):
         if p.is_alive():
             p.kill()
     assert (tmp_path / 'rank0.txt').read_text() != 'None'
+
+
+def test_plan_edge_cases():
+    """No requests, one request past the token budget (it goes alone), more ranks than requests."""
+    assert SH.plan_batches([], 16384) == []
+    assert SH.lpt_shard([], 4, 3) == []
+    assert SH.plan_batches([40000], 16384) == [[0]]
+    plan = SH.plan_batches([40000, 100, 120], 16384)
+    assert sorted(i for b in plan for i in b) == [0, 1, 2] and [0] in plan
+    shares = [SH.lpt_shard([300, 5000], 4, r) for r in range(4)]
+    assert sorted(i for s in shares for i in s) == [0, 1] and sum(1 for s in shares if not s) == 2
