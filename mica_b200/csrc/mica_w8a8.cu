@@ -420,6 +420,9 @@ static int gemm_plan(int M, int N, int K, int block_m, int block_n, int max_ctas
         if (bm == 256 && bn == 64) bn = 128;
         if (bm == 256 && bn == 320) bn = 256;
     }
+    // 128 x 320 tiles need one CTA per tile and take no K split: a capped grid, a forced cluster
+    // split or forced stream-K keeps the library's width choice at 256
+    if (block_n == 0 && bn == 320 && (max_ctas > 0 || splits > 1 || splits == MICA_SPLIT_STREAM_K)) bn = 256;
     p->bm = bm;
     p->bn = bn;
     p->streamk = false;
@@ -429,7 +432,7 @@ static int gemm_plan(int M, int N, int K, int block_m, int block_n, int max_ctas
     const long tiles = static_cast<long>((M + 127) / 128) * ((N + bn - 1) / bn);
     const int num_kb = (K + 127) / 128;
     if (splits == MICA_SPLIT_STREAM_K) {
-        if (bn == 64 || sms > 256) return MICA_ERR_UNSUPPORTED;
+        if ((bn != 128 && bn != 256) || sms > 256) return MICA_ERR_UNSUPPORTED;
         p->streamk = true;
     } else if (splits == 0 && (bn == 128 || bn == 256) && want_streamk(tiles, num_kb, sms)) {
         p->streamk = true;
