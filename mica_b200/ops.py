@@ -122,6 +122,19 @@ def _tile_args(tile: int):
 
 
 _WS_BYTES = {}
+_WS_CACHE_MAX = 4096       # shapes remembered; a server sees many token counts, so it is bounded
+
+
+def _workspace_bytes(device_index, m, n, k, tile):
+    """Workspace bytes of mica_w8a8_gemm_ex for this call (its device must be current),
+    remembered per (device, shape, tile); the memo is cleared when it reaches _WS_CACHE_MAX."""
+    key = (device_index, m, n, k, tile)
+    need = _WS_BYTES.get(key)
+    if need is None:
+        if len(_WS_BYTES) >= _WS_CACHE_MAX:
+            _WS_BYTES.clear()
+        need = _WS_BYTES[key] = int(N.lib().mica_w8a8_gemm_workspace_bytes(m, n, k, *_tile_args(tile)))
+    return need
 
 
 def _gemm(qx, sx, qw, sw, bias, out, out_code, tile):
@@ -131,10 +144,7 @@ def _gemm(qx, sx, qw, sw, bias, out, out_code, tile):
     n = qw.shape[0]
     args = _tile_args(tile)
     with _on(qx):
-        key = (qx.device.index, m, n, k, tile)
-        need = _WS_BYTES.get(key)
-        if need is None:
-            need = _WS_BYTES[key] = int(N.lib().mica_w8a8_gemm_workspace_bytes(m, n, k, *args))
+        need = _workspace_bytes(qx.device.index, m, n, k, tile)
         ws = torch.empty((need,), dtype=torch.uint8, device=qx.device) if need else None
         N.call('mica_w8a8_gemm_ex', qx.data_ptr(), qx.stride(0), qw.data_ptr(), qw.stride(0), sx.data_ptr(),
                sw.data_ptr(), _ptr(bias), out.data_ptr(), out_code, out.stride(0), m, n, k, *args,

@@ -169,3 +169,14 @@ def test_tile_codes_decode_to_the_c_arguments():
     assert _tile_args(1128064) == (128, 64, 0, 1)
     assert _tile_args(4128256) == (128, 256, 0, 4)
     assert _tile_args(9128256) == (128, 256, 0, N.SPLIT_STREAM_K)
+
+
+def test_workspace_size_memo_is_bounded():
+    """The per-shape memo of stream-K workspace sizes stays bounded however many token counts
+    a server sees (here the library answers 0: no device)."""
+    from mica_b200 import ops
+    ops._WS_BYTES.clear()
+    for m in range(1, ops._WS_CACHE_MAX + 500):
+        assert ops._workspace_bytes(0, m, 2560, 9728, 0) == 0
+    assert 0 < len(ops._WS_BYTES) <= ops._WS_CACHE_MAX
+    ops._WS_BYTES.clear()
