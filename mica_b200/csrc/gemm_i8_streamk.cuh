@@ -1,8 +1,8 @@
 // gemm_i8_streamk.cuh -- stream-K W8A8 GEMM for sm_100a: the last partial wave spread evenly.
 //
-// When a grid of 128 x BN tiles is a little more than a multiple of the SM count (config 0:
-// M 512 x N 9728 = 152 tiles of 128 x 256 on 148 SMs), the data-parallel kernel's critical
-// path is whole extra tiles. Here the G persistent CTAs (one per SM, co-resident: cooperative
+// When a grid of 128 x BN tiles is a little more than a multiple of the SM count (M 2048 x
+// N 3072 = 192 tiles of 128 x 256 on 148 SMs, too many for one wave even at 128 x 320), the
+// data-parallel kernel's critical path is whole extra tiles. Here the G persistent CTAs (one per SM, co-resident: cooperative
 // launch) share the tiles x k-blocks units equally: CTA c takes units
 // [c * U / G, (c + 1) * U / G), U = tiles * num_kb, in tile-major order. With tiles >= G every
 // CTA's run spans at least one tile's k-blocks, so a tile is cut at most once, between two
