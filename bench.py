@@ -41,6 +41,8 @@ from pathlib import Path
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
+from mica_b200.timing import graph_time  # noqa: E402
+
 PROJECTIONS = (('qkv', 6144, 2560), ('o', 2560, 4096), ('gate_up', 19456, 2560), ('down', 2560, 9728))
 MS = (256, 2048, 8192, 32768)
 OPS_PER_TOKEN = sum(2 * n * k for _, n, k in PROJECTIONS)   # 201.85 MOP per token per layer
@@ -352,12 +354,14 @@ def run_mica(args, rank, world, local):
     e2e_steps = max(1, min(args.steps, 5))
     e2e_ms = timed(e2e_step, e2e_steps, 2)
 
-    from mica_b200.shard import max_over_ranks
+    from mica_b200.shard import max_over_ranks, per_rank
+    ranks = per_rank([ms_total, e2e_ms, clocks['sm_mhz'] or 0.0], dev)
     ms_total, e2e_ms, gemm_ms = max_over_ranks([ms_total, e2e_ms, gemm_ms], dev)
     extra = {}
     if not args.skip_model:
         extra['config0_linear'] = run_linear(dev)
         extra['config2_chain'] = run_chain(dev)
+        extra['reference_gpu'] = run_reference_gpu(dev, weights, xs)
         extra.update(run_prefill(dev, rank, world))
     if rank != 0:
         return None
@@ -391,9 +395,22 @@ def run_mica(args, rank, world, local):
                      'peak_source': f"2 x {pk['source']} bf16 dense ({pk['bf16']} TFLOP/s); nominal dense int8 4500",
                      'frac_of_nominal_4500': round(achieved / 4500.0, 4)},
         'clocks': clocks,
+        'per_rank': per_rank_report(ranks, args.steps, e2e_steps, h2d + d2h),
         'other_configs': extra,
     }
     return line
+
+
+def per_rank_report(ranks, steps, e2e_steps, e2e_bytes):
+    """Each rank's sweep time and median SM clock, and the clock-free cost ms x MHz (so a
+    scaling curve can be read at equal clocks), plus each rank's host-link rate in the e2e run
+    (every e2e byte crosses the host link once; the box total is the sum)."""
+    sweep = [r[0] / steps for r in ranks]
+    mhz = [r[2] for r in ranks]
+    link = [e2e_bytes * e2e_steps / (r[1] * 1e-3) / 1e9 for r in ranks]
+    return {'sweep_ms_per_step': [round(v, 4) for v in sweep], 'sm_mhz': mhz,
+            'sweep_ms_x_mhz': [round(a * b, 1) for a, b in zip(sweep, mhz)],
+            'e2e_host_link_gbs': [round(v, 2) for v in link], 'e2e_box_host_link_gbs': round(sum(link), 2)}
 
 
 # ---------------------------------------------------------------------------------------
@@ -426,7 +443,7 @@ def run_chain(dev, reps=20):
         _, qh, sh = torch.ops.mica.gemm_swiglu_quant(q, s, wgu, sgu, None, None, 0)
         return torch.ops.mica.w8a8_gemm(qh, sh, wd, sd, None, 0, 0)
 
-    us = _graph_time(dev, chain, reps)
+    us = graph_time(dev, chain, reps)
     ops = 2 * M * 2 * I * H + 2 * M * H * I
     return {'config': 'config2: M=4096 RMSNorm+quant -> gate_up+SwiGLU+requant -> down', 'us_per_chain': round(us, 1),
             'gemm_tops': round(ops / us / 1e6, 1), 'launches_per_chain': 3}
@@ -451,8 +468,8 @@ def run_linear(dev, reps=20):
     def gemm():
         return torch.ops.mica.w8a8_gemm(q, s, w, sw, None, 0, 0)
 
-    us_lin = _graph_time(dev, linear, reps)
-    us_gemm = _graph_time(dev, gemm, reps)
+    us_lin = graph_time(dev, linear, reps)
+    us_gemm = graph_time(dev, gemm, reps)
     ops = 2 * M * N_ * K_
     gemm_bytes = M * K_ + N_ * K_ + 2 * M * N_ + 4 * (M + N_)
     pk = peaks()
@@ -464,32 +481,54 @@ def run_linear(dev, reps=20):
             'gemm_bytes': gemm_bytes, 'peaks': pk['source']}
 
 
-def _graph_time(dev, fn, reps):
-    """Mean device time of fn() over `reps` replays of one graph holding [L2 flush, event,
-    fn, event] per rep (events bracket fn exactly; the flush evicts L2 between reps)."""
+def reference_linear(x, qw, sw):
+    """The reference's W8A8 linear as it runs on a B200 for the BASELINE projection shapes, whose
+    (N, K) have no sm100 cubin specialisation (O's 2560 x 4096 is the one that has): QLinear's
+    torch fallback, v0.5/serving/lib/int8_runtime.py:181-192 -- int8_quant.quant_act
+    (lib/int8_quant.py:64-74), torch_int_mm (:92-97, torch._int_mm on cuBLASLt), the fp32
+    dequant and the bf16 cast -- as the same torch calls, restated."""
     import torch
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
-    ev = [(torch.cuda.Event(enable_timing=True, external=True), torch.cuda.Event(enable_timing=True, external=True))
-          for _ in range(reps)]
-    s2 = torch.cuda.Stream(device=dev)
-    s2.wait_stream(torch.cuda.current_stream(dev))
-    with torch.cuda.stream(s2):
-        for _ in range(3):
-            fn()
-    torch.cuda.current_stream(dev).wait_stream(s2)
-    g2 = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g2):
-        for a, b in ev:
-            flush.fill_(1)
-            a.record()
-            fn()
-            b.record()
-    g2.replay()
-    g2.replay()
-    torch.cuda.synchronize(dev)
-    t = sum(a.elapsed_time(b) for a, b in ev) / reps * 1e3
-    del g2
-    return t
+    xf = x.float()
+    s = xf.abs().amax(-1).clamp_min(1e-8) / 127.0
+    q = torch.round(xf / s[:, None]).clamp(-127, 127).to(torch.int8)
+    y = torch._int_mm(q, qw.t()).float() * s[:, None] * sw[None, :]
+    return y.to(torch.bfloat16)
+
+
+def run_reference_gpu(dev, weights, xs, reps=5):
+    """The reference's own GPU path on the same B200, per config-1 shape: reference_linear()
+    against this library's linear (act_quant + W8A8 GEMM), each graph-timed from a cold L2;
+    plus the library int8 GEMM alone (torch._int_mm, cuBLASLt) beside this library's GEMM,
+    which gives an empirical int8 library peak. The reference's Triton mm_i8 / act_quant cannot
+    run here: the reference is a Python tree with no package metadata (pip cannot install it)
+    and its source does not travel to the GPU box."""
+    import torch
+    rows, tot = [], {'ref': 0.0, 'mica': 0.0, 'ops': 0}
+    for m in MS:
+        for name, n, k in PROJECTIONS:
+            x = xs[m, k]
+            w, sw = weights[name]
+            q, s = torch.ops.mica.act_quant(x, None, 0)
+            ops = 2 * m * n * k
+            t_ref = graph_time(dev, lambda: reference_linear(x, w, sw), reps)
+            t_mica = graph_time(dev, lambda: torch.ops.mica.w8a8_gemm(*torch.ops.mica.act_quant(x, None, 0), w, sw,
+                                                                      None, 0, 0), reps)
+            t_lib = graph_time(dev, lambda: torch._int_mm(q, w.t()), reps)
+            t_gemm = graph_time(dev, lambda: torch.ops.mica.w8a8_gemm(q, s, w, sw, None, 0, 0), reps)
+            rows.append({'m': m, 'proj': name, 'n': n, 'k': k, 'reference_us': round(t_ref, 1),
+                         'mica_us': round(t_mica, 1), 'speedup': round(t_ref / t_mica, 2),
+                         'int_mm_tops': round(ops / t_lib / 1e6, 1), 'mica_gemm_tops': round(ops / t_gemm / 1e6, 1)})
+            tot['ref'] += t_ref
+            tot['mica'] += t_mica
+            tot['ops'] += ops
+    return {'what': 'reference QLinear torch path on CUDA (quant_act + torch._int_mm + fp32 dequant + bf16) vs '
+                    'this library (act_quant + W8A8 GEMM), per config-1 shape, graph-timed, L2 flushed',
+            'sweep_reference_tops': round(tot['ops'] / tot['ref'] / 1e6, 1),
+            'sweep_mica_tops': round(tot['ops'] / tot['mica'] / 1e6, 1),
+            'sweep_speedup': round(tot['ref'] / tot['mica'], 2),
+            'int8_library_gemm_peak_tops': max(r['int_mm_tops'] for r in rows),
+            'min_speedup_m_ge_2048': min(r['speedup'] for r in rows if r['m'] >= 2048),
+            'shapes': rows}
 
 
 def request_set(seed=4, n=256):
@@ -531,7 +570,7 @@ def run_prefill(dev, rank, world, batch_tokens=16384):
                           'prob_sum': round(float(p.sum()), 6)}
     # config 4: 256 requests sharded over the ranks; each rank scores its share in batches of
     # similar length (sorted, padded to 64-token buckets, up to batch_tokens rows per pass)
-    from mica_b200.shard import lpt_shard, max_over_ranks, plan_batches
+    from mica_b200.shard import lpt_shard, per_rank, plan_batches
     lengths, n_opts, req_ids = request_set()
     mine = lpt_shard(lengths, world, rank)
     batches = plan_batches([int(lengths[i]) for i in mine], batch_tokens)
@@ -555,10 +594,13 @@ def run_prefill(dev, rank, world, batch_tokens=16384):
     run_batches()
     b.record()
     b.synchronize()
-    ms_box = max_over_ranks([a.elapsed_time(b)], dev)[0]
+    busy = [r[0] for r in per_rank([a.elapsed_time(b)], dev)]
+    ms_box = max(busy)
     total = int(lengths.sum())
     out['config4_batch256'] = {'requests': len(lengths), 'tokens': total, 'ms_box': round(ms_box, 1),
                                'tokens_per_s_box': round(total / ms_box * 1e3),
+                               'busy_ms_per_rank': [round(v, 1) for v in busy],
+                               'busy_max_over_mean': round(max(busy) / (sum(busy) / len(busy)), 4),
                                'batches_rank0': len(batches), 'batch_graphs_rank0': len(shapes),
                                'batch_tokens': batch_tokens,
                                'sharding': f'LPT over {world} ranks, no collective'}

@@ -788,10 +788,10 @@ size_t mica_swiglu_workspace_bytes(int M) {
     return (static_cast<size_t>(M) * 4 + 15) / 16 * 16 + 16;
 }
 
-int mica_w8a8_gemm_swiglu_quant(const int8_t* A, long lda, const int8_t* Bgu, long ldb, const float* sa,
-                                const float* sgu, const float* bias_gu, const float* inv_h, void* h_out, long ldh,
-                                int8_t* q_out, long ldq, float* s_out, int M, int I, int K, int round_mode,
-                                void* workspace, size_t workspace_bytes, void* stream) {
+// Argument checks shared by the two fused SwiGLU entry points (no CUDA call is made).
+static int swiglu_args_ok(const int8_t* A, long lda, const int8_t* Bgu, long ldb, const float* sa, const float* sgu,
+                          const float* inv_h, const void* h_out, long ldh, const int8_t* q_out, long ldq,
+                          const float* s_out, int M, int I, int K, int round_mode) {
     if (!A || !Bgu || !sa || !sgu || !h_out || !q_out || !s_out || (round_mode != 0 && round_mode != 1))
         return MICA_ERR_ARG;
     if (M < 0 || I < 16 || (I & 15) || K < 16 || (K & 15) || lda < K || ldb < K || ldh < I || ldq < I)
@@ -800,6 +800,15 @@ int mica_w8a8_gemm_swiglu_quant(const int8_t* A, long lda, const int8_t* Bgu, lo
     if (!aligned16(A) || !aligned16(Bgu) || !aligned16(h_out) || !aligned16(q_out) || lda % 16 || ldb % 16 ||
         (ldh * 2) % 16 || ldq % 16 || (inv_h && !aligned16(inv_h)))
         return MICA_ERR_ALIGN;
+    return MICA_OK;
+}
+
+int mica_w8a8_gemm_swiglu_quant(const int8_t* A, long lda, const int8_t* Bgu, long ldb, const float* sa,
+                                const float* sgu, const float* bias_gu, const float* inv_h, void* h_out, long ldh,
+                                int8_t* q_out, long ldq, float* s_out, int M, int I, int K, int round_mode,
+                                void* workspace, size_t workspace_bytes, void* stream) {
+    if (int arc = swiglu_args_ok(A, lda, Bgu, ldb, sa, sgu, inv_h, h_out, ldh, q_out, ldq, s_out, M, I, K, round_mode))
+        return arc;
     if (!workspace || !aligned16(workspace)) return workspace ? MICA_ERR_ALIGN : MICA_ERR_ARG;
     if (workspace_bytes < mica_swiglu_workspace_bytes(M)) return MICA_ERR_WORKSPACE;
     int sms = 0;
@@ -869,8 +878,11 @@ int mica_w8a8_gemm_swiglu_quant_noalloc(const int8_t* A, long lda, const int8_t*
                                         const float* sgu, const float* bias_gu, const float* inv_h, void* h_out,
                                         long ldh, int8_t* q_out, long ldq, float* s_out, int M, int I, int K,
                                         int round_mode, void* stream) {
+    // the same argument checks as the workspace entry point, before any CUDA call
+    int rc = swiglu_args_ok(A, lda, Bgu, ldb, sa, sgu, inv_h, h_out, ldh, q_out, ldq, s_out, M, I, K, round_mode);
+    if (rc) return rc;
     if (M > MICA_NOALLOC_MAX_ROWS) return MICA_ERR_WORKSPACE;   // beyond the fixed scratch: refuse up front
-    int rc = check_device(nullptr);
+    rc = check_device(nullptr);
     if (rc) return rc;
     void* scratch = nullptr;
     if ((rc = noalloc_scratch(&scratch))) return rc;

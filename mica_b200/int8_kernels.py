@@ -96,6 +96,11 @@ def preload(device=None):
     return n.value
 
 
+def gemm_tile(n, k, m, device=None):
+    """The tuning table's tile code for this GEMM on `device` (tiles.tile with its SM count)."""
+    return tiles.tile(n, k, m, caps(device).sm_count)
+
+
 def _round_code():
     return _ROUND_CODE[ROUND['mode']]
 
@@ -158,7 +163,7 @@ def mm_i8(qx, sx, qw, sw, bias=None, out_dtype=torch.bfloat16):
         return _miss('align')
     if m == 0:
         return qx.new_empty((0, n), dtype=out_dtype)
-    y = torch.ops.mica.w8a8_gemm(qx, sx, qw, sw, bias, ops.DTYPE_CODE[out_dtype], tiles.tile(n, k, m))
+    y = torch.ops.mica.w8a8_gemm(qx, sx, qw, sw, bias, ops.DTYPE_CODE[out_dtype], gemm_tile(n, k, m, qx.device))
     _launched()
     return y
 

@@ -35,9 +35,13 @@ class KernelMiss(RuntimeError):
 
 
 def quant_weight(w: torch.Tensor):
-    """Per-output-row int8 weights, the reference's int8_quant.quant_weight (lib/int8_quant.py:54-62)."""
+    """Per-output-row int8 weights, the reference's int8_quant.quant_weight (lib/int8_quant.py:54-62).
+    The scale divides by a tensor of 127s: torch on CUDA turns a division by a Python scalar
+    into a multiply by its rounded reciprocal, which can move a scale by one ulp from the
+    reference's (CPU) result; an elementwise tensor division is correctly rounded everywhere."""
     wf = w.float()
-    s = wf.abs().amax(1).clamp_min(EPS) / 127.0
+    amax = wf.abs().amax(1).clamp_min(EPS)
+    s = amax / torch.full_like(amax, 127.0)
     q = torch.round(wf / s[:, None]).clamp(-127, 127).to(torch.int8)
     return q, s
 

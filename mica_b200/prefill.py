@@ -398,7 +398,8 @@ class Prefill:
         return _Normed(q, s, inv0, y), h
 
     def _gemm(self, q, s, w, sw, bias=None):
-        return torch.ops.mica.w8a8_gemm(q, s, w, sw, bias, 0, K.tiles.tile(w.shape[0], w.shape[1], q.shape[0]))
+        tile = K.gemm_tile(w.shape[0], w.shape[1], q.shape[0], q.device)
+        return torch.ops.mica.w8a8_gemm(q, s, w, sw, bias, 0, tile)
 
     def _qkv_cols(self, lay, nq, lo, hi, rows=None):
         """Columns [lo, hi) of the q|k|v projection of the normed input `nq` (for `rows` only,
@@ -415,7 +416,7 @@ class Prefill:
             q, s = nq.codes(inv, rows)
             w = lay.qkv_w[a:b]
             torch.ops.mica.w8a8_gemm_into(q, s, w, lay.qkv_s[a:b], None if bias is None else bias[a:b],
-                                          out[:, a - lo:b - lo], K.tiles.tile(w.shape[0], w.shape[1], m))
+                                          out[:, a - lo:b - lo], K.gemm_tile(w.shape[0], w.shape[1], m, q.device))
         return out
 
     def _attention(self, q, k, v, causal, mask=None):

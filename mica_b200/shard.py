@@ -84,6 +84,19 @@ def max_over_ranks(values, device='cpu'):
     return t.cpu().tolist()
 
 
+def per_rank(values, device='cpu') -> list:
+    """Every rank's `values` (a list of floats of the same length on each rank), indexed by
+    rank, on every rank: for reports of per-rank busy time, clocks and link rates."""
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([float(v) for v in values], dtype=torch.float64, device=device)
+    if not (dist.is_available() and dist.is_initialized() and dist.get_world_size() > 1):
+        return [t.cpu().tolist()]
+    out = [torch.empty_like(t) for _ in range(dist.get_world_size())]
+    dist.all_gather(out, t)
+    return [o.cpu().tolist() for o in out]
+
+
 def gather_to_rank0(local: dict, world: int):
     """Joins per-rank {request index: result} maps: rank 0 returns the union ordered by request
     index, other ranks None. Raises if two ranks report the same request."""

@@ -3,7 +3,11 @@
 Run in the build container, where the reference checkout is available (it is read, never
 copied; only inputs/outputs are saved):
 
-    python tests/golden/make_golden.py [/path/to/reference] [set names, e.g. model_int8]
+    python tests/golden/make_golden.py /path/to/reference [set names, e.g. model_int8]
+
+(or set MICA_REFERENCE to the reference checkout and name only the sets). The set
+`model_full` (the BASELINE-scale decoder of full_model.py scored at 2048 and 32768 tokens,
+about half an hour of CPU) is made only when named.
 
 What runs (all on CPU):
   * the reference's Triton kernels v0.5/serving/kernel_src/kernels.py act_quant and mm_i8,
@@ -28,7 +32,14 @@ import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
 HERE = Path(__file__).resolve().parent
-REF = Path(sys.argv[1] if len(sys.argv) > 1 else '/root/reference')
+ARGS = sys.argv[1:]
+if ARGS and Path(ARGS[0]).is_dir():
+    REF = Path(ARGS.pop(0))
+elif os.environ.get('MICA_REFERENCE'):
+    REF = Path(os.environ['MICA_REFERENCE'])
+else:
+    sys.exit('usage: make_golden.py /path/to/reference [sets...]  (or set MICA_REFERENCE)')
+sys.path.insert(0, str(HERE))
 sys.path.insert(0, str(REF / 'v0.5' / 'serving' / 'lib'))
 sys.path.insert(0, str(REF / 'v0.5' / 'serving' / 'kernel_src'))
 
@@ -302,6 +313,49 @@ def model_int8_cases(g):
     return {'m': out}
 
 
+@torch.no_grad()
+def model_full_cases(layers=None, lengths=None):
+    """The BASELINE-scale decoder of full_model.py (4B dims, 36 layers, vocab 151936) scored
+    the reference way: HF Qwen3ForCausalLM (bf16, SDPA attention) with every projection
+    converted by the reference's int8_runtime.convert (QLinear 'emulate': quant_act
+    half-even + exact int GEMM + dequant, lib/int8_runtime.py:172-206), the final norm's
+    last row, an fp32 linear over the 257 gathered rows (release_runtime.py:302-306) and
+    the softmax over the 255 options (:509-522). Only ids, rows, hidden state, logits and
+    probabilities are saved; the weights are regenerated from full_model.SEED."""
+    import time
+    import full_model as FM
+    from transformers import Qwen3Config, Qwen3ForCausalLM
+    from transformers.models.qwen3.modeling_qwen3 import Qwen3RotaryEmbedding
+    dims = dict(FM.HF_CONFIG)
+    if layers is not None:
+        dims['num_hidden_layers'] = layers
+    cfg = Qwen3Config(**dims)
+    cfg._attn_implementation = 'sdpa'
+    with torch.device('meta'):
+        model = Qwen3ForCausalLM(cfg)
+    model.load_state_dict(FM.state(cfg.num_hidden_layers), assign=True)
+    model.model.rotary_emb = Qwen3RotaryEmbedding(cfg)      # fp32 inv_freq, built off the meta device
+    model.eval()
+    bad = [n for n, t in list(model.named_parameters()) + list(model.named_buffers()) if t.is_meta]
+    assert not bad, bad
+    replaced, _ = rt.convert(model.model, None, 'emulate')
+    assert replaced == 7 * cfg.num_hidden_layers
+    out = {}
+    for n in (lengths or FM.LENGTHS):
+        ids, rows = FM.request(n)
+        t0 = time.time()
+        hid = model.model(ids[None]).last_hidden_state[:, -1]
+        weight = model.lm_head.weight.detach().index_select(0, rows).float()
+        z = torch.nn.functional.linear(hid.float(), weight).float()
+        lo, hi = FM.OPTION_SLICE
+        p = torch.zeros_like(z)
+        p[:, lo:hi] = z[:, lo:hi].softmax(-1)
+        print(f'model_full: {n} tokens in {time.time() - t0:.0f} s', flush=True)
+        out[f'n{n}'] = dict(ids=ids.numpy().astype(np.int32), rows=rows.numpy().astype(np.int32), hidden=bits(hid),
+                            logits=z.numpy(), probs=p.numpy(), slice=np.array([lo, hi], np.int32))
+    return out
+
+
 def save(name, cases):
     flat = {f'{c}/{k}': v for c, d in cases.items() for k, v in d.items()}
     np.savez_compressed(HERE / f'{name}.npz', **flat)
@@ -310,7 +364,7 @@ def save(name, cases):
 
 if __name__ == '__main__':
     # optional names after the reference path regenerate only those sets
-    only = set(sys.argv[2:])
+    only = set(ARGS)
     g = torch.Generator().manual_seed(20261201)
     for name, fn in (('act_quant', act_cases), ('gemm', gemm_cases), ('norm', norm_cases),
                      ('readout', readout_cases), ('selftest', selftest_cases), ('model', model_cases)):
@@ -319,3 +373,5 @@ if __name__ == '__main__':
             save(name, cases)
     if not only or 'model_int8' in only:
         save('model_int8', model_int8_cases(torch.Generator().manual_seed(20261203)))
+    if 'model_full' in only:
+        save('model_full', model_full_cases())

@@ -75,5 +75,13 @@ def test_entry_points_reject_bad_arguments_without_touching_a_gpu(lib_path):
     assert lib.mica_w8a8_gemm_workspace_bytes(512, 9728, 2560, 0, 0, 0, 0) == 0      # no device here
     assert lib.mica_w8a8_gemm_swiglu_quant(16, 32, 16, 32, 16, 16, None, None, 16, 32, 16, 32, 16, 4, 32, 32, 0,
                                            16, 8, None) == 7                                   # workspace
+    # the allocation-free SwiGLU entry point checks its arguments like the workspace one, then its
+    # row limit, all before any CUDA call
+    na = lib.mica_w8a8_gemm_swiglu_quant_noalloc
+    assert na(None, 32, 16, 32, 16, 16, None, None, 16, 32, 16, 32, 16, 4, 32, 32, 0, None) == 1   # ERR_ARG
+    assert na(16, 32, 16, 32, 16, 16, None, None, 16, 32, 16, 32, 16, 4, 32, 32, 3, None) == 1     # round mode
+    assert na(16, 32, 16, 32, 16, 16, None, None, 16, 32, 16, 32, 16, 4, 24, 32, 0, None) == 2     # I % 16
+    assert na(17, 32, 16, 32, 16, 16, None, None, 16, 32, 16, 32, 16, 4, 32, 32, 0, None) == 3     # misaligned
+    assert na(16, 32, 16, 32, 16, 16, None, None, 16, 32, 16, 32, 16, 65537, 32, 32, 0, None) == 7  # rows > limit
     assert lib.mica_option_logits(16, 0, 64, None, 0, 1e-6, 16, 0, 64, None, None, 16, 16, 1, None) == 2
     assert lib.mica_selftest_wait_timeout(None, 10, None) == 1

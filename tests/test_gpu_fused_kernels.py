@@ -1,0 +1,155 @@
+"""fused_kernels drop-in (the reference's v0.5/serving/lib/fused_kernels.py surface) and the
+BASELINE config-2 chain end to end.
+
+rms_norm / swi_glu are called exactly as the reference runtime calls them
+(lib/fork.py:179-187 rms_norm_fused, lib/fast_runtime.py:126-132 _fused_mlp) and compared
+with the reference's own outputs (tests/golden/norm.npz: its CPU branch and its Triton
+kernel). The config-2 chain (RMSNorm -> quant -> gate_up + SwiGLU + requant -> down at
+M = 4096 with x50 outliers) is compared with the oracle chain restating
+lib/fused_kernels.py:11-44 and lib/fast_runtime.py:126-132 with QLinear.forward."""
+import numpy as np
+import pytest
+import torch
+
+from conftest import ORACLE as O
+from conftest import golden
+
+pytestmark = pytest.mark.gpu
+
+
+def _bf16(a):
+    return torch.from_numpy(np.ascontiguousarray(a).view(np.int16)).view(torch.bfloat16)
+
+
+def _bits(t):
+    return t.contiguous().cpu().view(torch.int16).numpy().view(np.uint16)
+
+
+@pytest.mark.parametrize('case', ['a', 'b', 'c'])
+def test_rms_norm_drop_in_matches_reference_goldens(case):
+    from mica_b200 import fused_kernels as ffk
+    g = golden('norm')
+    x = _bf16(g[f'{case}/x']).cuda()
+    r = g[f'{case}/r']
+    res = _bf16(r).cuda() if r.size else None
+    w = _bf16(g[f'{case}/w']).cuda()
+    eps = float(g[f'{case}/eps'])
+    out = ffk.rms_norm(x, w, eps, res)
+    y, summed = out if res is not None else (out, None)
+    assert isinstance(out, tuple) == (res is not None)
+    assert y.shape == x.shape and y.dtype == x.dtype
+    ulp = np.abs(_bits(y).astype(int) - g[f'{case}/y_cpu'].astype(int))
+    assert ulp.max() <= 1 and (ulp > 0).mean() < 0.01
+    # the reference Triton kernel's fp32 output, rounded once
+    tri = O.f32_to_bf16_bits(g[f'{case}/y_triton_f32'])
+    ulp = np.abs(_bits(y).astype(int) - tri.astype(int))
+    assert ulp.max() <= 1 and (ulp > 0).mean() < 0.01
+    if res is not None:
+        assert np.array_equal(_bits(summed), g[f'{case}/sum_cpu'])
+
+
+def test_rms_norm_drop_in_nd_input_and_errors():
+    """[B, S, D] input with a residual (the runtime's call shape), against the oracle's
+    restatement of the reference CPU branch; a non-unit feature stride raises ValueError."""
+    from mica_b200 import fused_kernels as ffk
+    gen = torch.Generator().manual_seed(41)
+    x = torch.randn(3, 37, 2560, generator=gen).to(torch.bfloat16)
+    r = torch.randn(3, 37, 2560, generator=gen).to(torch.bfloat16)
+    w = (0.1 * torch.randn(2560, generator=gen)).to(torch.bfloat16)
+    y, summed = ffk.rms_norm(x.cuda(), w.cuda(), 1e-6, r.cuda())
+    assert y.shape == x.shape and summed.shape == x.shape
+    yo, so = O.rms_norm(x.float().numpy(), w.float().numpy(), 1e-6, r.float().numpy(), style='offset')
+    assert np.array_equal(summed.float().cpu().numpy(), so)
+    ulp = np.abs(_bits(y).astype(int) - O.f32_to_bf16_bits(yo).astype(int))
+    assert ulp.max() <= 1 and (ulp > 0).mean() < 0.01
+    y1 = ffk.rms_norm(x.cuda(), w.cuda(), 1e-6)
+    assert y1.shape == x.shape and not isinstance(y1, tuple)
+    # a row-strided view (every other row of a wider buffer) is served like its copy
+    wide = torch.randn(40, 2 * 2560, generator=gen).to(torch.bfloat16).cuda()
+    view = wide[:, :2560]
+    assert torch.equal(ffk.rms_norm(view, w.cuda(), 1e-6), ffk.rms_norm(view.contiguous(), w.cuda(), 1e-6))
+    with pytest.raises(ValueError):
+        ffk.rms_norm(wide.t(), w.cuda()[:40].contiguous(), 1e-6)
+    with pytest.raises(RuntimeError):
+        ffk.rms_norm(x.cuda(), w.float().cuda(), 1e-6)       # weight of another dtype
+
+
+def test_swi_glu_drop_in_matches_reference_goldens():
+    from mica_b200 import fused_kernels as ffk
+    g = golden('norm')
+    gate, up = _bf16(g['swiglu/g']).cuda(), _bf16(g['swiglu/u']).cuda()
+    h = ffk.swi_glu(gate, up)
+    assert h.shape == gate.shape and h.dtype == gate.dtype
+    # the reference's CPU branch (its Triton kernel rounds silu(g) to bf16 inside the kernel,
+    # which Triton's CPU interpreter truncates, so that golden is not compared here)
+    hk = O.bf16_bits_to_f32(_bits(h))
+    hr = O.bf16_bits_to_f32(g['swiglu/y_cpu'])
+    assert np.allclose(hk, hr, rtol=1e-2, atol=1e-2 * np.abs(hr).max())
+    assert (hk != hr).mean() < 0.01
+    # [B, S, I] projections, and a width that is not a multiple of 8 (served as rows of 8)
+    gen = torch.Generator().manual_seed(5)
+    for shape in ((2, 33, 9728), (5, 12)):
+        a = (3 * torch.randn(shape, generator=gen)).to(torch.bfloat16)
+        b = torch.randn(shape, generator=gen).to(torch.bfloat16)
+        hk = ffk.swi_glu(a.cuda(), b.cuda()).float().cpu().numpy()
+        hr = O.silu_mul(a.float().numpy(), b.float().numpy())
+        assert hk.shape == tuple(shape)
+        assert np.allclose(hk, hr, rtol=1e-2, atol=1e-2 * np.abs(hr).max())
+        assert (hk != hr).mean() < 0.01
+    with pytest.raises(ValueError):
+        ffk.swi_glu(gate.t(), up.t())
+
+
+# ---------------------------------------------------------------------------------------
+def test_config2_chain_matches_oracle():
+    """BASELINE config 2 as bench.py runs it: x N(0,1) [4096, 2560] bf16 with 0.1 % of the
+    elements of 8 seeded channels x50, gamma N(1, 0.1), eps 1e-6; RMSNorm + quant, gate_up
+    GEMM + SwiGLU + requant, down GEMM (three launches). Codes and scales after the norm are
+    bit-exact given the kernel's y; h and the down output within 1e-2 relative of the
+    oracle chain run end to end from x."""
+    from mica_b200 import _native as Nat
+    from mica_b200.int8_runtime import interleave_gate_up
+    M, H, I = 4096, 2560, 9728
+    gen = torch.Generator().manual_seed(2)
+    x = torch.randn(M, H, generator=gen)
+    ch = torch.randperm(H, generator=gen)[:8]
+    n_out = round(0.001 * M * H)
+    rows = torch.randint(0, M, (n_out,), generator=gen)
+    cols = ch[torch.randint(0, 8, (n_out,), generator=gen)]
+    x[rows, cols] *= 50
+    x = x.to(torch.bfloat16)
+    gamma = (1 + 0.1 * torch.randn(H, generator=gen)).to(torch.bfloat16)
+    wg = torch.randint(-127, 128, (I, H), generator=gen, dtype=torch.int8)
+    wu = torch.randint(-127, 128, (I, H), generator=gen, dtype=torch.int8)
+    sg = torch.rand(I, generator=gen) * 9e-3 + 1e-3
+    su = torch.rand(I, generator=gen) * 9e-3 + 1e-3
+    wd = torch.randint(-127, 128, (H, I), generator=gen, dtype=torch.int8)
+    sd = torch.rand(H, generator=gen) * 9e-3 + 1e-3
+    dev = torch.device('cuda')
+    wgu, sgu = interleave_gate_up(wg.to(dev), wu.to(dev)), interleave_gate_up(sg.to(dev), su.to(dev))
+
+    q, s, y, _ = torch.ops.mica.rmsnorm_quant(x.to(dev), None, gamma.to(dev), None, 1e-6, Nat.NORM_WEIGHT, 0, True,
+                                              True)
+    h, qh, sh = torch.ops.mica.gemm_swiglu_quant(q, s, wgu, sgu, None, None, 0)
+    out = torch.ops.mica.w8a8_gemm(qh, sh, wd.to(dev), sd.to(dev), None, 0, 0)
+    torch.cuda.synchronize()
+
+    # the norm: within the HF double rounding of the oracle; codes exact given y
+    yo, _ = O.rms_norm(x.float().numpy(), gamma.float().numpy(), 1e-6, None, style='weight')
+    yk = y.float().cpu().numpy()
+    ulp = np.abs(O.f32_to_bf16_bits(yk).astype(int) - O.f32_to_bf16_bits(yo).astype(int))
+    assert ulp.max() <= 2 and (ulp > 0).mean() < 0.01
+    q2, s2 = O.quant_act_half_away(yk)
+    assert np.array_equal(q.cpu().numpy(), q2) and np.array_equal(s.cpu().numpy(), s2)
+    # the oracle chain end to end from x
+    qo, so = O.quant_act_half_away(yo)
+    ho, qho, sho = O.gate_up_swiglu_quant(qo, so, wg.numpy(), sg.numpy(), wu.numpy(), su.numpy())
+    hk = h.float().cpu().numpy()
+    assert np.allclose(hk, ho, rtol=1e-2, atol=1e-2 * np.abs(ho).max())
+    outo = O.dequant_out(O.int_gemm_exact(qho, wd.numpy()), sho, sd.numpy())
+    ok = out.float().cpu().numpy()
+    assert np.allclose(ok, outo, rtol=1e-2, atol=1e-2 * np.abs(outo).max())
+    # the requantisation is bit-exact given the kernel's own h, and so is the down GEMM
+    q3, s3 = O.quant_act_half_away(hk)
+    assert np.array_equal(qh.cpu().numpy(), q3) and np.array_equal(sh.cpu().numpy(), s3)
+    assert np.array_equal(ok, O.dequant_out(O.int_gemm_exact(q3, wd.numpy()), s3, sd.numpy()))

@@ -180,3 +180,50 @@ def test_workspace_size_memo_is_bounded():
         assert ops._workspace_bytes(0, m, 2560, 9728, 0) == 0
     assert 0 < len(ops._WS_BYTES) <= ops._WS_CACHE_MAX
     ops._WS_BYTES.clear()
+
+
+def test_fused_kernels_drop_in_has_no_cpu_path():
+    """fused_kernels.rms_norm / swi_glu keep the reference's names and arguments but, unlike
+    the reference module, serve CUDA tensors only: a CPU tensor raises RuntimeError (which
+    the reference's caller, fork.rms_norm_fused, catches) instead of computing on the CPU."""
+    from mica_b200 import fused_kernels as ffk
+    x = torch.zeros(2, 3, 64, dtype=torch.bfloat16)
+    w = torch.zeros(64, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match='CUDA'):
+        ffk.rms_norm(x, w, 1e-6)
+    with pytest.raises(RuntimeError, match='CUDA'):
+        ffk.rms_norm(x, w, 1e-6, torch.zeros_like(x))
+    with pytest.raises(RuntimeError, match='CUDA'):
+        ffk.swi_glu(x, x)
+    import inspect
+    assert list(inspect.signature(ffk.rms_norm).parameters) == ['x', 'weight', 'eps', 'residual']
+    assert list(inspect.signature(ffk.swi_glu).parameters) == ['gate', 'up']
+
+
+def test_tile_codes_the_tuner_weighs_are_all_valid_and_the_table_drops_others(tmp_path):
+    """The tuner's candidates cover every kind of tile the library has (library choice,
+    128-row 64/128/256/320, CTA pairs, never-split, forced K splits 2..8, stream-K); a state
+    file's unknown codes are ignored, and a 320-wide entry applies only where its grid fits
+    one wave (elsewhere the call takes the library's choice)."""
+    from mica_b200 import tiles
+    assert all(tiles.valid(c) for c in tiles.CHOICES)
+    kinds = {c // 1000000 for c in tiles.CHOICES}
+    assert kinds == set(range(0, 9)) | {9}
+    assert 128320 in tiles.CHOICES and 0 in tiles.CHOICES and 256256 in tiles.CHOICES
+    for bad in (-1, 128000, 128512, 256064, 256320, 2256256, 2128320, 9128064, 10128128, 128096):
+        assert not tiles.valid(bad), bad
+    assert all(tiles.valid(v) for v in tiles._load(tiles.PINNED).values())
+    (tmp_path / tiles.STATE_NAME).write_text(
+        '{"format": "mica-tiles/1", "entries": {"mm|N64|K64|cs": 2256256, "mm|N64|K64|cm": "x", '
+        '"mm|N9728|K2560|cm": 128320, "mm|N64|K64|cl": 9128256}}')
+    loaded = tiles._load(tmp_path / tiles.STATE_NAME)
+    assert loaded == {'mm|N9728|K2560|cm': 128320, 'mm|N64|K64|cl': 9128256}
+    tiles.set_state_dir(tmp_path)
+    try:
+        assert tiles.tile(9728, 2560, 300, sms=148) == 128320       # 3 x 31 = 93 tiles: one wave
+        assert tiles.tile(9728, 2560, 384, sms=148) == 128320
+        assert tiles.effective(128320, 9728, 640, 148) == 0           # 5 x 31 = 155 tiles
+        assert tiles.tile(9728, 2560, 300) == 128320                   # no SM count: as stored
+        assert tiles.tile(64, 64, 5000, sms=148) == 9128256
+    finally:
+        tiles.set_state_dir(None)

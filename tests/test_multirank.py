@@ -55,6 +55,7 @@ def _worker(rank, port, out_dir):
         dist.all_gather_object(shares, mine)
         # timing: the box's time is the slowest rank's
         t = SH.max_over_ranks([10.0 + rank, 5.0 - rank])
+        every = SH.per_rank([10.0 + rank, 5.0 - rank])
         # results: scored here, gathered on rank 0 in request order
         batches = SH.plan_batches([lengths[i] for i in mine], 16384)
         local = {}
@@ -63,7 +64,7 @@ def _worker(rank, port, out_dir):
                 i = mine[j]
                 local[i] = _fake_score(i, lengths[i])
         res = SH.gather_to_rank0(local, WORLD)
-        torch.save({'mine': mine, 'shares': shares, 't': t, 'res': res, 'batches': batches},
+        torch.save({'mine': mine, 'shares': shares, 't': t, 'every': every, 'res': res, 'batches': batches},
                    Path(out_dir) / f'rank{rank}.pt')
     finally:
         dist.destroy_process_group()
@@ -81,6 +82,7 @@ def test_two_gloo_ranks_partition_reduce_and_gather(tmp_path):
     loads = [sum(SH.request_cost(lengths[i]) for i in m) for m in (r0['mine'], r1['mine'])]
     assert abs(loads[0] - loads[1]) <= max(SH.request_cost(L) for L in lengths)
     assert r0['t'] == r1['t'] == [11.0, 5.0]
+    assert r0['every'] == r1['every'] == [[10.0, 5.0], [11.0, 4.0]]
     assert r0['res'] == [_fake_score(i, L) for i, L in enumerate(lengths)]
     assert r1['res'] is None
     # each rank's batches cover its requests once, within the token budget
@@ -120,6 +122,7 @@ def test_plan_is_the_single_process_plan():
     lengths = _lengths()
     assert SH.lpt_shard(lengths, 1, 0) == list(range(len(lengths)))
     assert SH.max_over_ranks([3.0, 4.0]) == [3.0, 4.0]
+    assert SH.per_rank([3.0, 4.0]) == [[3.0, 4.0]]
     assert SH.gather_to_rank0({2: 'b', 0: 'a'}, 1) == ['a', 'b']
     with pytest.raises(ValueError):
         SH.lpt_shard(lengths, 2, 2)

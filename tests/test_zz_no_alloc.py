@@ -97,3 +97,17 @@ def test_noalloc_rejects_rows_beyond_its_fixed_scratch(lib):
                                                         i, dummy.data_ptr(), m, i, k, 0,
                                                         torch.cuda.current_stream().cuda_stream)
     assert rc == 7   # MICA_ERR_WORKSPACE
+
+
+@pytest.mark.parametrize('m,i,k', [(2048, 9728, 2560), (65536, 64, 64)])
+def test_noalloc_matches_workspace_entry_point_at_its_limits(lib, m, i, k):
+    """A grid large enough for the 256-wide tiles, and the maximum row count, where the grid
+    barrier's counter sits in the last bytes of the fixed scratch; codes and scales exact."""
+    x = _inputs(m, i, k, seed=3 + m, x_scale=1.0)
+    a = _call_noalloc(lib, *x, m, i, k)
+    b = _call_workspace(lib, *x, m, i, k)
+    torch.cuda.synchronize()
+    _close(a, b)
+    code = ctypes.c_int(-1)
+    lib.call('mica_device_error', ctypes.byref(code), torch.cuda.current_stream().cuda_stream)
+    assert code.value == 0
