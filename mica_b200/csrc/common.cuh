@@ -67,16 +67,34 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
+// As mbar_try_wait, but a thread whose phase is not complete sleeps in hardware until the
+// phase completes or about kSleepHintNs pass. A polling loop of non-blocking tests keeps the
+// shared-memory pipe busy with barrier probes; on B200 that slowed a CTA pair's stage
+// hand-off (MMA commit -> empty barrier -> producer -> full barrier -> MMA) by a fifth, where
+// the sleeping form wakes on the phase change and keeps the tensor pipe fed.
+constexpr uint32_t kSleepHintNs = 1000000;   // 1 ms; a completed phase ends the sleep at once
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "n"(kSleepHintNs)
+        : "memory");
+    return ok != 0;
+}
+
 // Bounded wait on phase `parity` of `bar`. Returns false when the CTA-wide abort flag is
-// raised or the wait outlives kWaitLimitNs (then it raises the flag and records `code`).
+// raised or the wait outlives limit_ns (then it raises the flag and records `code`).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile uint32_t* abort_flag,
                                           int code, unsigned long long limit_ns = kWaitLimitNs) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_sleep(bar, parity)) return true;
     const unsigned long long t0 = global_ns();
-    for (uint32_t it = 0;; ++it) {
-        if (mbar_try_wait(bar, parity)) return true;
+    for (;;) {
+        if (mbar_try_wait_sleep(bar, parity)) return true;
         if (*abort_flag) return false;
-        if ((it & 15u) == 15u && global_ns() - t0 > limit_ns) {
+        if (global_ns() - t0 > limit_ns) {
             *abort_flag = 1u;
             atomicExch(&g_dev_error, code);
             return false;
@@ -231,6 +249,27 @@ __device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_
         : "memory");
 }
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+// ---- packed fp32 pairs (sm_100 f32x2 arithmetic: two IEEE round-to-nearest operations per
+// instruction, no contraction, so each lane equals the scalar __fmul_rn / __fadd_rn) --------
+__device__ __forceinline__ unsigned long long f2_pack(float lo, float hi) {
+    unsigned long long v;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(v) : "f"(lo), "f"(hi));
+    return v;
+}
+__device__ __forceinline__ void f2_unpack(unsigned long long v, float& lo, float& hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ unsigned long long f2_mul(unsigned long long a, unsigned long long b) {
+    unsigned long long r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ unsigned long long f2_add(unsigned long long a, unsigned long long b) {
+    unsigned long long r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+
 // Ties 32 registers written by tcgen05.ld to this point of the program, so no use of them is
 // scheduled above the tcgen05.wait::ld that precedes it (emits no instruction).
 __device__ __forceinline__ void reg_pin32(uint32_t (&r)[32]) {

@@ -127,6 +127,93 @@ __device__ __forceinline__ void dequant_chunk_to_box(const uint32_t (&r)[32], fl
     }
 }
 
+// True when a chunk's 32 column scales (and biases) can be read as 16-byte vectors: the chunk
+// lies inside N and both vectors are 16-byte aligned at its first column.
+__device__ __forceinline__ bool chunk_vectorisable(const GemmArgs& a, int col, int N) {
+    const uintptr_t bits = reinterpret_cast<uintptr_t>(a.sb + col) |
+                           (a.bias != nullptr ? reinterpret_cast<uintptr_t>(a.bias + col) : 0u);
+    return col + 32 <= N && (bits & 15u) == 0;
+}
+
+// The dequant epilogue of one whole 32-column chunk on packed fp32 pairs: the same
+// y = (acc * sa) * sb (+ bias) per element, each step one IEEE round-to-nearest operation, as
+// dequant_chunk_to_box, but the column scales arrive as eight uniform 16-byte loads (served
+// from L1 after the first warp) instead of 32 shuffles, and every multiply covers two columns.
+// sb4 holds the chunk's 32 scales; biasp is the chunk's first bias or nullptr.
+template <typename OutT>
+__device__ __forceinline__ void dequant_chunk_packed(const uint32_t (&r)[32], float sa_v, const float4 (&sb4)[8],
+                                                     const float* biasp, uint32_t box_row, int cc) {
+    const int lane = threadIdx.x & 31;
+    const unsigned long long sa2 = f2_pack(sa_v, sa_v);
+    unsigned long long y2[16];
+#pragma unroll
+    for (int v = 0; v < 8; ++v) {
+        const unsigned long long a0 = f2_pack(__int2float_rn(static_cast<int>(r[4 * v])),
+                                              __int2float_rn(static_cast<int>(r[4 * v + 1])));
+        const unsigned long long a1 = f2_pack(__int2float_rn(static_cast<int>(r[4 * v + 2])),
+                                              __int2float_rn(static_cast<int>(r[4 * v + 3])));
+        y2[2 * v] = f2_mul(f2_mul(a0, sa2), f2_pack(sb4[v].x, sb4[v].y));
+        y2[2 * v + 1] = f2_mul(f2_mul(a1, sa2), f2_pack(sb4[v].z, sb4[v].w));
+    }
+    if (biasp != nullptr) {
+#pragma unroll
+        for (int v = 0; v < 8; ++v) {
+            const float4 b4 = __ldg(reinterpret_cast<const float4*>(biasp) + v);
+            y2[2 * v] = f2_add(y2[2 * v], f2_pack(b4.x, b4.y));
+            y2[2 * v + 1] = f2_add(y2[2 * v + 1], f2_pack(b4.z, b4.w));
+        }
+    }
+    if constexpr (sizeof(OutT) == 2) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            float lo, hi;
+            f2_unpack(y2[j], lo, hi);
+            if constexpr (std::is_same<OutT, __half>::value) pk[j] = pack_f16(lo, hi);
+            else pk[j] = pack_bf16(lo, hi);
+        }
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const int chunk = cc * 4 + c;
+            st_shared_v4(box_row + ((chunk ^ (lane & 7)) << 4), pk[4 * c], pk[4 * c + 1], pk[4 * c + 2],
+                         pk[4 * c + 3]);
+        }
+    } else {
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+            float a, b, d, e;
+            f2_unpack(y2[2 * c], a, b);
+            f2_unpack(y2[2 * c + 1], d, e);
+            st_shared_v4(box_row + ((c ^ (lane & 7)) << 4), __float_as_uint(a), __float_as_uint(b),
+                         __float_as_uint(d), __float_as_uint(e));
+        }
+    }
+}
+
+// One 32-column chunk of the dequant epilogue: tensor-memory load of the lane's row, then the
+// packed form when the chunk's column vectors allow it, else the gathered form.
+template <typename OutT>
+__device__ __forceinline__ void dequant_chunk(const GemmArgs& args, uint32_t t_addr, int gcol0, int N, float sa_v,
+                                              uint32_t box_row, int cc) {
+    const int lane = threadIdx.x & 31;
+    uint32_t r[32];
+    if (chunk_vectorisable(args, gcol0, N)) {
+        float4 sb4[8];
+#pragma unroll
+        for (int v = 0; v < 8; ++v) sb4[v] = __ldg(reinterpret_cast<const float4*>(args.sb + gcol0) + v);
+        tmem_ld_32x32b_x32(t_addr, r);
+        tmem_ld_wait();
+        dequant_chunk_packed<OutT>(r, sa_v, sb4, args.bias != nullptr ? args.bias + gcol0 : nullptr, box_row, cc);
+    } else {
+        const int gcol = gcol0 + lane;
+        const float sb_l = gcol < N ? args.sb[gcol] : 0.f;
+        const float bias_l = (args.bias != nullptr && gcol < N) ? args.bias[gcol] : 0.f;
+        tmem_ld_32x32b_x32(t_addr, r);
+        tmem_ld_wait();
+        dequant_chunk_to_box<OutT>(r, sa_v, sb_l, bias_l, args.bias != nullptr, box_row, cc);
+    }
+}
+
 // f[e] = RN(f[e] * inv[e]) for eight consecutive columns (inv 16-byte aligned).
 __device__ __forceinline__ void scale8(float (&f)[8], const float* inv) {
     const float4 a = __ldg(reinterpret_cast<const float4*>(inv));
@@ -270,45 +357,45 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
         __syncwarp();
     } else if (warp == 1) {
         // ------------------------------- MMA issuer ---------------------------------
-        constexpr uint32_t idesc = idesc_i8(S::BM, S::MMA_N);
-        const uint32_t a_base = smem_u32(smem_a);
-        const uint32_t b_base = smem_u32(smem_b);
-        uint32_t it = 0;
-        int local = 0;
-        bool ok = true;
-        for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
-            const int acc = local & 1;
-            const uint32_t acc_ph = (local >> 1) & 1;
-            bool w = true;
-            if (lane == 0) w = mbar_wait(&tempty_bar[acc], acc_ph ^ 1u, abort_flag, MICA_DEV_TIMEOUT_MMA);
-            if (!__shfl_sync(0xffffffffu, w, 0)) { ok = false; break; }
-            tc_fence_after();
-            const uint32_t d_tmem = tmem_base + acc * S::ACC_COLS;
-            for (int kb = 0; kb < num_kb; ++kb, ++it) {
-                const int st = it % STAGES;
-                const uint32_t ph = (it / STAGES) & 1u;
-                if (lane == 0) w = mbar_wait(&full_bar[st], ph, abort_flag, MICA_DEV_TIMEOUT_MMA);
-                if (!__shfl_sync(0xffffffffu, w, 0)) { ok = false; break; }
+        // One lane runs the whole loop: per stage a wait on its full barrier, the k-step MMAs
+        // and a commit that frees the stage. The TMA bytes' completion on the barrier orders the
+        // shared-memory tiles before the MMAs; a tcgen05 fence is needed only after taking an
+        // accumulator back from the epilogue warps.
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_i8(S::BM, S::MMA_N);
+            // descriptors of stage 0; a stage / k-step is a plain offset of the address field
+            const uint64_t a_desc0 = smem_desc_k128(smem_u32(smem_a));
+            const uint64_t b_desc0 = smem_desc_k128(smem_u32(smem_b));
+            uint32_t it = 0;
+            int local = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
+                const int acc = local & 1;
+                const uint32_t acc_ph = (local >> 1) & 1;
+                if (!mbar_wait(&tempty_bar[acc], acc_ph ^ 1u, abort_flag, MICA_DEV_TIMEOUT_MMA)) break;
                 tc_fence_after();
-                if (lane == 0) {
-                    const uint32_t a_addr = a_base + st * S::A_BYTES;
-                    const uint32_t b_addr = b_base + st * S::B_BYTES;
+                const uint32_t d_tmem = tmem_base + acc * S::ACC_COLS;
+                for (int kb = 0; kb < num_kb; ++kb, ++it) {
+                    const int st = it % STAGES;
+                    if (!mbar_wait(&full_bar[st], (it / STAGES) & 1u, abort_flag, MICA_DEV_TIMEOUT_MMA)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint64_t a_st = a_desc0 + static_cast<uint64_t>((st * S::A_BYTES) >> 4);
+                    const uint64_t b_st = b_desc0 + static_cast<uint64_t>((st * S::B_BYTES) >> 4);
 #pragma unroll
                     for (int k = 0; k < S::BK / S::UMMA_K; ++k) {
 #pragma unroll
                         for (int hf = 0; hf < S::HALVES; ++hf)
-                            mma_i8(d_tmem + hf * S::MMA_N, smem_desc_k128(a_addr + k * S::UMMA_K),
-                                   smem_desc_k128(b_addr + hf * S::MMA_N * S::BK + k * S::UMMA_K), idesc,
+                            mma_i8(d_tmem + hf * S::MMA_N, a_st + static_cast<uint64_t>((k * S::UMMA_K) >> 4),
+                                   b_st + static_cast<uint64_t>((hf * S::MMA_N * S::BK + k * S::UMMA_K) >> 4), idesc,
                                    (kb | k) != 0 ? 1u : 0u);
                     }
                     mma_commit(&empty_bar[st]);          // frees the stage when these MMAs finish
                     if (kb == num_kb - 1) mma_commit(&tfull_bar[acc]);  // accumulator complete
                 }
-                __syncwarp();
             }
-        }
-        // Drain: every MMA issued must finish before tensor memory is released.
-        if (lane == 0) {
+            // Drain: every MMA issued must finish before tensor memory is released.
             mma_commit(drain_bar);
             mbar_wait(drain_bar, 0, abort_flag, MICA_DEV_TIMEOUT_DRAIN);
         }
@@ -356,13 +443,7 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
 #pragma unroll
                     for (int cc = 0; cc < CHUNKS_PER_BOX; ++cc) {
                         const int col0 = bx * COLS_PER_BOX + cc * 32;
-                        const int gcol = n0 + col0 + lane;
-                        const float sb_l = gcol < N ? args.sb[gcol] : 0.f;
-                        const float bias_l = (args.bias != nullptr && gcol < N) ? args.bias[gcol] : 0.f;
-                        uint32_t r[32];
-                        tmem_ld_32x32b_x32(t_row + col0, r);
-                        tmem_ld_wait();
-                        dequant_chunk_to_box<OutT>(r, sa_v, sb_l, bias_l, args.bias != nullptr, box_row, cc);
+                        dequant_chunk<OutT>(args, t_row + col0, n0 + col0, N, sa_v, box_row, cc);
                     }
                     if (bx + PARTS >= BOXES) {
                         // this warp's last read of the accumulator: hand it back to the MMA warp

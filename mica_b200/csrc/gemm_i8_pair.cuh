@@ -4,20 +4,24 @@
 // tcgen05.mma.cta_group::2.kind::i8 instructions (256 x BN x 32 each) issued by the even
 // CTA. Each CTA holds 128 rows of A and BN/2 rows of B per stage in its own shared memory
 // (at identical offsets), so per SM the MMA reads 16 KB of A and 16 KB of B per 128-byte K
-// step instead of 16 + 32 KB in the single-CTA kernel: a third less shared-memory and L2
-// traffic for the same work, and room for six stages instead of four.
+// step instead of 16 + 32 KB in the single-CTA kernel. A 128 x 256 single-CTA MMA asks the
+// shared memory for 96 bytes per clock of operands while TMA writes the next stages at the
+// same rate, more than its bandwidth; on pairs both halve, which is what lets this tile keep
+// the tensor pipe busy.
 //
-// The even CTA's producer issues all four loads of a stage: the .cta_group::2 TMA form
-// writes the odd CTA's half into its shared memory and still completes on the even CTA's
-// barrier. Every stage completion is then local to the MMA issuer. When each CTA loaded its
-// own half, the odd CTA's two completions per stage crossed the pair and, on B200, cost the
-// main loop about a seventh of its rate. The odd CTA runs no producer.
+// Loads: each CTA's producer issues its own two loads per stage (its A rows and its half of
+// B) into its own shared memory, and both complete their bytes on the EVEN CTA's full
+// barrier, which the even producer arms with the pair's byte count (.cta_group::2 TMA; a
+// byte count may land before the arming, the transaction count is signed). So every SM's
+// TMA unit moves 32 KB per stage, and the MMA issuer waits on one local barrier.
+// The MMA commit of a stage arrives on both CTAs' empty barriers (two commits), so each
+// producer refills its own stages as soon as the pair's MMAs are done with them.
 //
 // Synchronisation (all waits bounded, as in gemm_i8.cuh):
-//   full[s]    even CTA: its four TMA loads of the stage complete their bytes on it;
-//   empty[s]   even CTA: the MMA commit of the stage arrives on it;
+//   full[s]    even CTA: the pair's four TMA loads of the stage complete their bytes on it;
+//   empty[s]   per CTA: the even CTA's MMA commit of the stage arrives on both copies;
 //   tfull[a]   per CTA: the even CTA's last commit of a tile arrives on both copies;
-//   tempty[a]  even CTA only: all 256 epilogue threads of the pair arrive on it.
+//   tempty[a]  even CTA only: one arrival per epilogue warp of the pair (8).
 // Epilogue and semantics are those of gemm_i8_kernel (dequant, no FMA, TMA store).
 #pragma once
 
@@ -90,7 +94,7 @@ gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&tfull_bar[i], 1);
-            mbar_init(&tempty_bar[i], 2 * S::EPI_WARPS * 32);
+            mbar_init(&tempty_bar[i], 2 * S::EPI_WARPS);
         }
         mbar_init(drain_bar, 1);
         *abort_flag = 0u;
@@ -106,8 +110,8 @@ gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
     const uint32_t tmem_base = *tmem_slot;
 
     if (warp == 0) {
-        // ------------------------------- TMA producer (even CTA) ---------------------
-        if (leader && lane == 0) {
+        // ------------------------------- TMA producers (both CTAs) -------------------
+        if (lane == 0) {
             uint32_t it = 0;
             bool ok = true;
             const uint64_t pol_b = policy_evict_last();
@@ -122,72 +126,65 @@ gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
                         ok = false;
                         break;
                     }
-                    const uint32_t full = smem_u32(&full_bar[st]);
-                    const uint32_t a_st = smem_u32(smem_a + st * S::A_BYTES);
-                    const uint32_t b_st = smem_u32(smem_b + st * S::B_BYTES);
-                    mbar_arrive_expect_tx(&full_bar[st], 2 * S::STAGE_BYTES);
-                    for (uint32_t r = 0; r < 2; ++r) {
-                        tma_load_2d_pair(map_to_rank(a_st, r), &tmap_a, full, kb * S::BK,
-                                         m0 + static_cast<int>(r) * 128, pol_a);
-                        tma_load_2d_pair(map_to_rank(b_st, r), &tmap_b, full, kb * S::BK,
-                                         n0 + static_cast<int>(r) * (BN / 2), pol_b);
-                    }
+                    const uint32_t full = map_to_rank(smem_u32(&full_bar[st]), 0);
+                    if (leader) mbar_arrive_expect_tx(&full_bar[st], 2 * S::STAGE_BYTES);
+                    tma_load_2d_pair(map_to_rank(smem_u32(smem_a + st * S::A_BYTES), rank), &tmap_a, full,
+                                     kb * S::BK, m0 + static_cast<int>(rank) * 128, pol_a);
+                    tma_load_2d_pair(map_to_rank(smem_u32(smem_b + st * S::B_BYTES), rank), &tmap_b, full,
+                                     kb * S::BK, n0 + static_cast<int>(rank) * (BN / 2), pol_b);
                 }
             }
-            // Drain: the pair's last loads of each stage land before shared memory goes away
-            // (the odd CTA waits for this warp at the closing cluster barrier).
+            // Drain: every stage this CTA loaded has been consumed by the pair's MMAs (so its
+            // bytes have landed) before the CTA reaches the closing cluster barrier.
             const uint32_t first = it > static_cast<uint32_t>(STAGES) ? it - STAGES : 0u;
-            for (uint32_t j = first; j < it; ++j)
-                mbar_wait(&full_bar[j % STAGES], (j / STAGES) & 1u, abort_flag, MICA_DEV_TIMEOUT_DRAIN);
+            for (uint32_t j = first; j < it && ok; ++j)
+                mbar_wait(&empty_bar[j % STAGES], (j / STAGES) & 1u, abort_flag, MICA_DEV_TIMEOUT_DRAIN);
         }
         __syncwarp();
     } else if (warp == 1) {
         // ------------------------------- MMA issuer (even CTA) -----------------------
-        if (leader) {
+        // One lane runs the loop (see gemm_i8_kernel): a wait per stage, the k-step MMAs, a
+        // commit to both CTAs' empty barriers; a tcgen05 fence only per accumulator hand-back.
+        if (leader && lane == 0) {
             constexpr uint32_t idesc = idesc_i8(S::BM, BN);
-            const uint32_t a_base = smem_u32(smem_a);
-            const uint32_t b_base = smem_u32(smem_b);
+            const uint64_t a_desc0 = smem_desc_k128(smem_u32(smem_a));
+            const uint64_t b_desc0 = smem_desc_k128(smem_u32(smem_b));
             uint32_t it = 0;
             int local = 0;
             bool ok = true;
             for (int tile = cluster_id; tile < num_tiles && ok; tile += num_clusters, ++local) {
                 const int acc = local & 1;
                 const uint32_t acc_ph = (local >> 1) & 1;
-                bool w = true;
-                if (lane == 0) w = mbar_wait(&tempty_bar[acc], acc_ph ^ 1u, abort_flag, MICA_DEV_TIMEOUT_MMA);
-                if (!__shfl_sync(0xffffffffu, w, 0)) { ok = false; break; }
+                if (!mbar_wait(&tempty_bar[acc], acc_ph ^ 1u, abort_flag, MICA_DEV_TIMEOUT_MMA)) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + acc * S::ACC_COLS;
                 for (int kb = 0; kb < num_kb; ++kb, ++it) {
                     const int st = it % STAGES;
-                    const uint32_t ph = (it / STAGES) & 1u;
-                    if (lane == 0) w = mbar_wait(&full_bar[st], ph, abort_flag, MICA_DEV_TIMEOUT_MMA);
-                    if (!__shfl_sync(0xffffffffu, w, 0)) { ok = false; break; }
-                    tc_fence_after();
-                    if (lane == 0) {
-                        const uint32_t a_addr = a_base + st * S::A_BYTES;
-                        const uint32_t b_addr = b_base + st * S::B_BYTES;
-#pragma unroll
-                        for (int k = 0; k < S::BK / S::UMMA_K; ++k) {
-                            mma_i8_pair(d_tmem, smem_desc_k128(a_addr + k * S::UMMA_K),
-                                        smem_desc_k128(b_addr + k * S::UMMA_K), idesc, (kb | k) != 0 ? 1u : 0u);
-                        }
-                        mma_commit_pair(map_to_rank(smem_u32(&empty_bar[st]), 0));
-                        if (kb == num_kb - 1) {
-                            const uint32_t f = smem_u32(&tfull_bar[acc]);
-                            mma_commit_pair(map_to_rank(f, 0));
-                            mma_commit_pair(map_to_rank(f, 1));
-                        }
+                    if (!mbar_wait(&full_bar[st], (it / STAGES) & 1u, abort_flag, MICA_DEV_TIMEOUT_MMA)) {
+                        ok = false;
+                        break;
                     }
-                    __syncwarp();
+                    const uint64_t a_st = a_desc0 + static_cast<uint64_t>((st * S::A_BYTES) >> 4);
+                    const uint64_t b_st = b_desc0 + static_cast<uint64_t>((st * S::B_BYTES) >> 4);
+#pragma unroll
+                    for (int k = 0; k < S::BK / S::UMMA_K; ++k) {
+                        mma_i8_pair(d_tmem, a_st + static_cast<uint64_t>((k * S::UMMA_K) >> 4),
+                                    b_st + static_cast<uint64_t>((k * S::UMMA_K) >> 4), idesc, (kb | k) != 0 ? 1u : 0u);
+                    }
+                    const uint32_t e = smem_u32(&empty_bar[st]);
+                    mma_commit_pair(map_to_rank(e, 0));
+                    mma_commit_pair(map_to_rank(e, 1));
+                    if (kb == num_kb - 1) {
+                        const uint32_t f = smem_u32(&tfull_bar[acc]);
+                        mma_commit_pair(map_to_rank(f, 0));
+                        mma_commit_pair(map_to_rank(f, 1));
+                    }
                 }
             }
-            if (lane == 0) {
-                mma_commit_pair(map_to_rank(smem_u32(drain_bar), 0));
-                mbar_wait(drain_bar, 0, abort_flag, MICA_DEV_TIMEOUT_DRAIN);
-            }
-            __syncwarp();
+            mma_commit_pair(map_to_rank(smem_u32(drain_bar), 0));
+            mbar_wait(drain_bar, 0, abort_flag, MICA_DEV_TIMEOUT_DRAIN);
         }
+        __syncwarp();
     } else {
         // ------------------------------- epilogue (both CTAs) ------------------------
         const int q4 = warp & 3;
@@ -221,47 +218,13 @@ gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
 #pragma unroll
                 for (int cc = 0; cc < CHUNKS_PER_BOX; ++cc) {
                     const int col0 = bx * COLS_PER_BOX + cc * 32;
-                    const int gcol = n0 + col0 + lane;
-                    const float sb_l = gcol < N ? args.sb[gcol] : 0.f;
-                    const float bias_l = (args.bias != nullptr && gcol < N) ? args.bias[gcol] : 0.f;
-                    uint32_t r[32];
-                    tmem_ld_32x32b_x32(t_row + col0, r);
-                    tmem_ld_wait();
-                    float y[32];
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const float sbj = __shfl_sync(0xffffffffu, sb_l, j);
-                        y[j] = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[j])), sa_v), sbj);
-                    }
-                    if (args.bias != nullptr) {
-#pragma unroll
-                        for (int j = 0; j < 32; ++j) y[j] = __fadd_rn(y[j], __shfl_sync(0xffffffffu, bias_l, j));
-                    }
-                    if constexpr (sizeof(OutT) == 2) {
-                        uint32_t p[16];
-#pragma unroll
-                        for (int j = 0; j < 16; ++j) {
-                            if constexpr (std::is_same<OutT, __half>::value) p[j] = pack_f16(y[2 * j], y[2 * j + 1]);
-                            else p[j] = pack_bf16(y[2 * j], y[2 * j + 1]);
-                        }
-#pragma unroll
-                        for (int c = 0; c < 4; ++c) {
-                            const int chunk = cc * 4 + c;
-                            st_shared_v4(box_row + ((chunk ^ (lane & 7)) << 4), p[4 * c], p[4 * c + 1], p[4 * c + 2],
-                                         p[4 * c + 3]);
-                        }
-                    } else {
-#pragma unroll
-                        for (int c = 0; c < 8; ++c) {
-                            st_shared_v4(box_row + ((c ^ (lane & 7)) << 4), __float_as_uint(y[4 * c]),
-                                         __float_as_uint(y[4 * c + 1]), __float_as_uint(y[4 * c + 2]),
-                                         __float_as_uint(y[4 * c + 3]));
-                        }
-                    }
+                    dequant_chunk<OutT>(args, t_row + col0, n0 + col0, N, sa_v, box_row, cc);
                 }
                 if (bx == BOXES - 1) {
+                    // this warp's last read of the accumulator: one arrival for the warp
                     tc_fence_before();
-                    mbar_arrive_cluster(map_to_rank(smem_u32(&tempty_bar[acc]), 0));
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive_cluster(map_to_rank(smem_u32(&tempty_bar[acc]), 0));
                 }
                 fence_proxy_async_smem();
                 __syncwarp();

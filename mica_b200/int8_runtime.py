@@ -15,6 +15,8 @@ Differences, by design:
 """
 from __future__ import annotations
 
+from dataclasses import dataclass
+
 import torch
 from torch import nn
 
@@ -325,116 +327,168 @@ def write_int8_file(path, tensors: dict, ties: dict | None = None):
 
 
 def target_linears(body, layers=None, modules=None):
-    """(qualified name, parent, attr, Linear) for every projection in `body.layers`
-    (reference lib/int8_quant.py:99-110)."""
-    names = GROUPS['all'] if modules is None else tuple(modules)
-    wanted = range(len(body.layers)) if layers is None else layers
-    out = []
-    for i in wanted:
+    """Every projection Linear of `body.layers` (the reference's int8_quant.target_linears,
+    lib/int8_quant.py:99-110): a list of (name 'layers.<i>.<path>', parent module, attribute,
+    Linear), layer by layer in module order."""
+    names = frozenset(GROUPS['all'] if modules is None else modules)
+    picked = range(len(body.layers)) if layers is None else layers
+    found = []
+    for i in picked:
         layer = body.layers[i]
-        for path, parent in layer.named_modules():
-            for attr, child in parent.named_children():
-                if attr in names and isinstance(child, nn.Linear):
-                    out.append((f'layers.{i}.{path + "." if path else ""}{attr}', parent, attr, child))
-    return out
+        for path, mod in layer.named_modules():
+            owner, _, leaf = path.rpartition('.')
+            if leaf in names and isinstance(mod, nn.Linear):
+                found.append((f'layers.{i}.{path}', layer.get_submodule(owner) if owner else layer, leaf, mod))
+    return found
+
+
+def _smoothing(stats, name, linear, alpha):
+    """SmoothQuant factors of one projection from its activation statistics, or None."""
+    amax = None if stats is None else stats.get(name)
+    return None if amax is None else smooth_factors(amax, linear.weight.detach(), alpha)
 
 
 def convert(body, stats, backend='aot', alpha=ALPHA, keep_bf16=False, fuse_mlp=False):
-    """Replace every projection Linear with QLinear (reference :195-206). With fuse_mlp,
-    each `mlp` that has gate/up/down projections becomes a FusedMLP instead.
-    Returns (replaced, smoothed)."""
+    """Swaps every projection Linear of the decoder body for a QLinear, smoothed where `stats`
+    holds that projection's activation maxima (the reference's int8_runtime.convert,
+    lib/int8_runtime.py:195-206). With fuse_mlp each `mlp` holding gate/up/down Linears becomes
+    one FusedMLP first. Returns (projections replaced, projections smoothed)."""
     replaced = smoothed = 0
     if fuse_mlp:
         for i, layer in enumerate(body.layers):
             mlp = getattr(layer, 'mlp', None)
-            if mlp is not None and all(isinstance(getattr(mlp, n, None), nn.Linear) for n in MLP):
-                layer.mlp = FusedMLP(mlp, stats, f'layers.{i}.mlp.', alpha)
-                replaced += 3
-                smoothed += layer.mlp.inv_smooth is not None
-    for qname, parent, attr, child in target_linears(body):
-        amax = stats.get(qname) if stats is not None else None
-        smooth = None if amax is None else smooth_factors(amax, child.weight.detach(), alpha)
-        setattr(parent, attr, QLinear(child, smooth, backend, keep_bf16=keep_bf16))
+            if mlp is None or not all(isinstance(getattr(mlp, n, None), nn.Linear) for n in MLP):
+                continue
+            layer.mlp = FusedMLP(mlp, stats, f'layers.{i}.mlp.', alpha)
+            replaced += len(MLP)
+            smoothed += int(layer.mlp.inv_smooth is not None)
+    for name, parent, attr, linear in target_linears(body):
+        smooth = _smoothing(stats, name, linear, alpha)
+        parent.register_module(attr, QLinear(linear, smooth, backend, keep_bf16=keep_bf16))
         replaced += 1
-        smoothed += smooth is not None
-        del child
-    return (replaced, smoothed)
+        smoothed += int(smooth is not None)
+    return replaced, smoothed
 
 
 # ---------------------------------------------------------------------------------------
-# Start-up self-test, the reference's int8_runtime.selftest (lib/int8_runtime.py:362-443):
-# random weights per (N, K, bias) shape, a smoothed and an unsmoothed QLinear, the reference
-# rows; the kernels' output must be within 1.05x the INT8 emulation noise of the bf16
-# product, and every call must launch the library's kernels (2 per linear).
+# Start-up self-test (the reference's int8_runtime.selftest, lib/int8_runtime.py:288-443):
+# before serving, every projection shape runs through this library's act_quant + mm_i8 on
+# seeded data, smoothed and unsmoothed, at several row counts; each result must stay within
+# SELFTEST_TOL times the error an exact INT8 emulation makes against the bf16 product, and
+# every case must launch the library's two kernels. The seed, the rows and the tolerance are
+# the reference's; the data recipe and the code are this library's.
 SELFTEST_ROWS = (3, 48, 200, 608, 1500)
 SELFTEST_TOL = 1.05
 SELFTEST_SEED = 20261022
 
 
-def _row_rel(a, b):
-    return float(((a - b).norm(dim=-1) / b.norm(dim=-1).clamp_min(1e-30)).max())
+@dataclass(frozen=True)
+class SelfTestCase:
+    n: int
+    k: int
+    bias: bool
+    smoothed: bool
+    m: int
+
+
+def selftest_plan(shapes, rows=SELFTEST_ROWS):
+    """The cases for these (N, K, has_bias) shapes: each shape smoothed and plain, at each row count."""
+    return [SelfTestCase(int(n), int(k), bool(b), sm, int(m)) for n, k, b in shapes for sm in (True, False)
+            for m in rows]
+
+
+def _worst_row_error(y, ref):
+    """Largest per-row relative L2 error of y against ref."""
+    err = (y - ref).norm(dim=-1) / ref.norm(dim=-1).clamp_min(1e-30)
+    return float(err.max())
+
+
+class _ShapeData:
+    """Seeded weights, channel ranges and bias of one (N, K, has_bias) shape, on the device:
+    weights N(0, 0.05) in bf16; per-channel activation ranges log-normal around 1 with one
+    channel in 50 twenty times wider (outlier channels, what smoothing is for)."""
+
+    def __init__(self, n, k, bias, gen, dev):
+        self.w = (torch.randn(n, k, generator=gen, device=dev) * 0.05).to(torch.bfloat16)
+        spread = torch.exp(0.5 * torch.randn(k, generator=gen, device=dev))
+        spread[torch.arange(0, k, 50, device=dev)] *= 20.0
+        self.spread = spread
+        self.bias = (torch.randn(n, generator=gen, device=dev) * 0.1).float() if bias else None
+        self.prepared = {}
+
+    def weights(self, smoothed):
+        """(qweight, wscale, inv_smooth or None, dequantised weight) of the projection."""
+        if smoothed not in self.prepared:
+            wf = self.w.float()
+            inv = None
+            if smoothed:
+                f = smooth_factors(self.spread, self.w, ALPHA)
+                wf = wf * f[None, :]
+                inv = (1.0 / f).contiguous()
+            qw, sw = quant_weight(wf)
+            w_eff = qw.float() * sw[:, None]
+            self.prepared[smoothed] = (qw, sw, inv, w_eff if inv is None else w_eff * inv[None, :])
+        return self.prepared[smoothed]
+
+
+def _emulated_linear(x, inv, qw, sw, bias):
+    """An exact W8A8 linear: per-token codes (round half even), exact integer products
+    (float64 on the device), fp32 dequant, cast to bf16."""
+    xf = x.float() if inv is None else x.float() * inv
+    amax = xf.abs().amax(-1).clamp_min(EPS)
+    s = amax / torch.full_like(amax, 127.0)
+    codes = torch.round(xf / s[:, None]).clamp(-127, 127)
+    y = (codes.double() @ qw.double().t()).float() * s[:, None] * sw[None, :]
+    return (y if bias is None else y + bias).to(torch.bfloat16).float()
 
 
 def selftest(shapes, device, rows=SELFTEST_ROWS):
-    """Returns {'ok', 'reason', 'checked', 'worst_ratio', 'launches', 'seconds'} like the
-    reference. The INT8 emulation runs on the device with exact float64 integer products."""
+    """Runs selftest_plan(shapes, rows) on `device`; returns the reference's report
+    {'ok', 'reason', 'checked', 'worst_ratio', 'launches', 'seconds'}. Never raises."""
     import time
-    import types
 
-    t0 = time.perf_counter()
-    out = {'ok': False, 'reason': '', 'checked': 0, 'worst_ratio': 0.0}
+    started = time.perf_counter()
+    report = {'ok': False, 'reason': '', 'checked': 0, 'worst_ratio': 0.0}
     try:
         dev = torch.device(device)
-        ok, why = aot.available(dev)
-        if not ok:
-            out['reason'] = why
-            return out
-        launches = aot.STATS['launch']
-        g = torch.Generator().manual_seed(SELFTEST_SEED)
-        for n, k, has_bias in shapes:
-            n, k = int(n), int(k)
-            w = (torch.randn(n, k, generator=g) * 0.05).to(torch.bfloat16)
-            amax = torch.rand(k, generator=g) * 4 + 0.05
-            amax[::61] *= 25.0
-            b = (torch.randn(n, generator=g) * 0.1).to(torch.bfloat16).to(dev) if has_bias else None
-            lin = types.SimpleNamespace(weight=w.to(dev), bias=b)
-            for smooth in (smooth_factors(amax, w, ALPHA), None):
-                q = QLinear(lin, smooth)
-                wd = q.qweight.float() * q.wscale[:, None]
-                if q.inv_smooth is not None:
-                    wd = wd * q.inv_smooth[None, :]
-                for m in rows:
-                    x = (torch.randn(m, k, generator=g) * amax / 3).to(torch.bfloat16).to(dev)
-                    l0 = aot.STATS['launch']
-                    y = q(x).float()
-                    if aot.STATS['launch'] - l0 < 2:
-                        out['reason'] = 'N %d K %d M %d: %d kernel launches (expected 2)' % (
-                            n, k, m, aot.STATS['launch'] - l0)
-                        return out
-                    ref = x.float() @ wd.t()
-                    xf = x.float() * q.inv_smooth if q.inv_smooth is not None else x.float()
-                    sx = xf.abs().amax(-1).clamp_min(EPS) / 127.0
-                    qx = torch.round(xf / sx[:, None]).clamp(-127, 127)
-                    acc = (qx.double() @ q.qweight.double().t()).round()
-                    emu = acc.float() * sx[:, None] * q.wscale[None, :]
-                    if q.bias is not None:
-                        ref, emu = ref + q.bias, emu + q.bias
-                    emu = emu.to(q.out_dtype).float()
-                    noise, err = _row_rel(emu, ref), _row_rel(y, ref)
-                    if not bool(torch.isfinite(y).all()):
-                        out['reason'] = 'non-finite output (N %d, K %d, M %d)' % (n, k, m)
-                        return out
-                    if not err <= SELFTEST_TOL * noise:
-                        out['reason'] = 'N %d K %d M %d: error %.4g > %.2f x INT8 noise %.4g' % (
-                            n, k, m, err, SELFTEST_TOL, noise)
-                        return out
-                    out['worst_ratio'] = max(out['worst_ratio'], err / max(noise, 1e-30))
-                    out['checked'] += 1
+        usable, why = aot.available(dev)
+        if not usable:
+            report['reason'] = why
+            return report
+        gen = torch.Generator(device=dev).manual_seed(SELFTEST_SEED)
+        first_launch = aot.STATS['launch']
+        data = {}
+        for case in selftest_plan(shapes, rows):
+            shape = (case.n, case.k, case.bias)
+            if shape not in data:
+                data[shape] = _ShapeData(*shape, gen, dev)
+            d = data[shape]
+            qw, sw, inv, w_eff = d.weights(case.smoothed)
+            x = (torch.randn(case.m, case.k, generator=gen, device=dev) * d.spread / 3).to(torch.bfloat16)
+            where = 'N %d K %d M %d%s' % (case.n, case.k, case.m, ' smoothed' if case.smoothed else '')
+            before = aot.STATS['launch']
+            qx = aot.act_quant(x, inv)
+            y = None if qx is None else aot.mm_i8(qx[0], qx[1], qw, sw, d.bias, torch.bfloat16)
+            if y is None or aot.STATS['launch'] - before != 2:
+                report['reason'] = f'{where}: the kernels did not serve the call ({aot.STATS["fallback"]})'
+                return report
+            y = y.float()
+            if not bool(torch.isfinite(y).all()):
+                report['reason'] = f'{where}: non-finite output'
+                return report
+            exact = x.float() @ w_eff.t() + (d.bias if d.bias is not None else 0.0)
+            noise = _worst_row_error(_emulated_linear(x, inv, qw, sw, d.bias), exact)
+            err = _worst_row_error(y, exact)
+            if err > SELFTEST_TOL * noise:
+                report['reason'] = f'{where}: error {err:.4g} > {SELFTEST_TOL:.2f} x INT8 noise {noise:.4g}'
+                return report
+            report['worst_ratio'] = max(report['worst_ratio'], err / max(noise, 1e-30))
+            report['checked'] += 1
         torch.cuda.synchronize(dev)
-        out.update(ok=True, reason='ok', launches=aot.STATS['launch'] - launches,
-                   worst_ratio=round(out['worst_ratio'], 5))
-    except Exception as exc:  # the reference reports, never raises
-        out['reason'] = ('%s: %s' % (type(exc).__name__, exc))[:300]
+        report.update(ok=True, reason='ok', launches=aot.STATS['launch'] - first_launch,
+                      worst_ratio=round(report['worst_ratio'], 5))
+    except Exception as exc:  # a start-up check reports; it never takes the server down
+        report['reason'] = f'{type(exc).__name__}: {exc}'[:300]
     finally:
-        out['seconds'] = round(time.perf_counter() - t0, 2)
-    return out
+        report['seconds'] = round(time.perf_counter() - started, 2)
+    return report

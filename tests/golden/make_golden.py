@@ -7,7 +7,8 @@ copied; only inputs/outputs are saved):
 
 (or set MICA_REFERENCE to the reference checkout and name only the sets). The set
 `model_full` (the BASELINE-scale decoder of full_model.py scored at 2048 and 32768 tokens,
-about half an hour of CPU) is made only when named.
+about half an hour of CPU) and `model_full_band` (the same with fp32 attention, the reference's
+own sensitivity to attention rounding) are made only when named.
 
 What runs (all on CPU):
   * the reference's Triton kernels v0.5/serving/kernel_src/kernels.py act_quant and mm_i8,
@@ -313,8 +314,22 @@ def model_int8_cases(g):
     return {'m': out}
 
 
+def _register_fp32_attention():
+    """'sdpa_fp32': HF's SDPA attention with q, k, v upcast to fp32 and the output cast back,
+    a more accurate attention than the served bf16 one, used to measure how far the reference
+    model's own probabilities move under an attention rounding change."""
+    from transformers import AttentionInterface
+    from transformers.integrations.sdpa_attention import sdpa_attention_forward
+
+    def fp32_forward(module, query, key, value, attention_mask, **kwargs):
+        out, w = sdpa_attention_forward(module, query.float(), key.float(), value.float(), attention_mask, **kwargs)
+        return out.to(query.dtype), w
+
+    AttentionInterface.register('sdpa_fp32', fp32_forward)
+
+
 @torch.no_grad()
-def model_full_cases(layers=None, lengths=None):
+def model_full_cases(layers=None, lengths=None, attn='sdpa'):
     """The BASELINE-scale decoder of full_model.py (4B dims, 36 layers, vocab 151936) scored
     the reference way: HF Qwen3ForCausalLM (bf16, SDPA attention) with every projection
     converted by the reference's int8_runtime.convert (QLinear 'emulate': quant_act
@@ -330,7 +345,9 @@ def model_full_cases(layers=None, lengths=None):
     if layers is not None:
         dims['num_hidden_layers'] = layers
     cfg = Qwen3Config(**dims)
-    cfg._attn_implementation = 'sdpa'
+    if attn == 'sdpa_fp32':
+        _register_fp32_attention()
+    cfg._attn_implementation = attn
     with torch.device('meta'):
         model = Qwen3ForCausalLM(cfg)
     model.load_state_dict(FM.state(cfg.num_hidden_layers), assign=True)
@@ -350,7 +367,7 @@ def model_full_cases(layers=None, lengths=None):
         lo, hi = FM.OPTION_SLICE
         p = torch.zeros_like(z)
         p[:, lo:hi] = z[:, lo:hi].softmax(-1)
-        print(f'model_full: {n} tokens in {time.time() - t0:.0f} s', flush=True)
+        print(f'model_full ({attn}): {n} tokens in {time.time() - t0:.0f} s', flush=True)
         out[f'n{n}'] = dict(ids=ids.numpy().astype(np.int32), rows=rows.numpy().astype(np.int32), hidden=bits(hid),
                             logits=z.numpy(), probs=p.numpy(), slice=np.array([lo, hi], np.int32))
     return out
@@ -375,3 +392,6 @@ if __name__ == '__main__':
         save('model_int8', model_int8_cases(torch.Generator().manual_seed(20261203)))
     if 'model_full' in only:
         save('model_full', model_full_cases())
+    if 'model_full_band' in only:
+        # the same model and requests with fp32 attention: the reference's own sensitivity
+        save('model_full_band', model_full_cases(attn='sdpa_fp32'))
