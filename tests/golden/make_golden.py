@@ -8,7 +8,8 @@ copied; only inputs/outputs are saved):
 (or set MICA_REFERENCE to the reference checkout and name only the sets). The set
 `model_full` (the BASELINE-scale decoder of full_model.py scored at 2048 and 32768 tokens,
 about half an hour of CPU) and `model_full_band` (the same with fp32 attention, the reference's
-own sensitivity to attention rounding) are made only when named.
+own sensitivity to attention rounding) and `model_layer0` (layer 0's intermediates at full dims)
+are made only when named.
 
 What runs (all on CPU):
   * the reference's Triton kernels v0.5/serving/kernel_src/kernels.py act_quant and mm_i8,
@@ -373,6 +374,52 @@ def model_full_cases(layers=None, lengths=None, attn='sdpa'):
     return out
 
 
+@torch.no_grad()
+def model_layer0_cases():
+    """Layer 0 of the BASELINE-scale decoder of full_model.py on the 2048-token request, as the
+    reference computes it (HF Qwen3 decoder layer, every projection a QLinear 'emulate',
+    SDPA attention): for the last 4 rows, the attention output that o_proj quantises, o_proj's
+    output, the post-attention norm, the SwiGLU product that down_proj quantises, down_proj's
+    output and the layer's output. Given the same attention output, every later step of a
+    layer is exact integer arithmetic plus single roundings, so a W8A8 layer can reproduce
+    these bit for bit."""
+    import full_model as FM
+    from transformers import Qwen3Config, Qwen3ForCausalLM
+    from transformers.models.qwen3.modeling_qwen3 import Qwen3RotaryEmbedding
+    dims = dict(FM.HF_CONFIG)
+    dims['num_hidden_layers'] = 1
+    cfg = Qwen3Config(**dims)
+    cfg._attn_implementation = 'sdpa'
+    with torch.device('meta'):
+        model = Qwen3ForCausalLM(cfg)
+    model.load_state_dict(FM.state(1), assign=True)
+    model.model.rotary_emb = Qwen3RotaryEmbedding(cfg)
+    model.eval()
+    rt.convert(model.model, None, 'emulate')
+    lay = model.model.layers[0]
+    cap = {}
+
+    def out_hook(name):
+        def hook(mod, inp, out):
+            cap[name] = (out[0] if isinstance(out, tuple) else out)[0, -4:].contiguous()
+        return hook
+
+    def in_hook(name):
+        def hook(mod, inp):
+            cap[name] = inp[0][0, -4:].contiguous()
+        return hook
+
+    lay.self_attn.o_proj.register_forward_pre_hook(in_hook('attn'))
+    lay.self_attn.o_proj.register_forward_hook(out_hook('o_proj'))
+    lay.post_attention_layernorm.register_forward_hook(out_hook('ln2'))
+    lay.mlp.down_proj.register_forward_pre_hook(in_hook('h'))
+    lay.mlp.down_proj.register_forward_hook(out_hook('down'))
+    lay.register_forward_hook(out_hook('layer_out'))
+    ids, _ = FM.request(2048)
+    model.model(ids[None])
+    return {'l0': {k: bits(v) for k, v in cap.items()}}
+
+
 def save(name, cases):
     flat = {f'{c}/{k}': v for c, d in cases.items() for k, v in d.items()}
     np.savez_compressed(HERE / f'{name}.npz', **flat)
@@ -392,6 +439,8 @@ if __name__ == '__main__':
         save('model_int8', model_int8_cases(torch.Generator().manual_seed(20261203)))
     if 'model_full' in only:
         save('model_full', model_full_cases())
+    if 'model_layer0' in only:
+        save('model_layer0', model_layer0_cases())
     if 'model_full_band' in only:
         # the same model and requests with fp32 attention: the reference's own sensitivity
         save('model_full_band', model_full_cases(attn='sdpa_fp32'))
