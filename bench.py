@@ -691,6 +691,24 @@ def run_shape(args):
         qw = gamma[:128].contiguous()
         fn = lambda: torch.ops.mica.qk_norm_rope(qkv, qw, qw, cos, sin, None, 0, 32, 8, 1e-6)  # noqa: E731
         work = ('GB/s', m * 5120 * 2 * 2)
+    elif args.kernel == 'compare':
+        # cuBLASLt's int8 GEMM (torch._int_mm, int32 out) beside this library's 128 x 256 and CTA-pair
+        # GEMMs on the same operands, once per step each; the timed steps run inside the NVTX range
+        # 'prof' so a profiler can take exactly those three launches (ncu --nvtx --nvtx-include prof/)
+        fns = [lambda: torch._int_mm(q, w.t()), lambda: torch.ops.mica.w8a8_gemm(q, s, w, sw, None, 0, 0),
+               lambda: torch.ops.mica.w8a8_gemm(q, s, w, sw, None, 0, 256256)]
+        for _ in range(args.warmup):
+            for f in fns:
+                f()
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_push('prof')
+        for _ in range(args.steps):
+            for f in fns:
+                f()
+        torch.cuda.nvtx.range_pop()
+        torch.cuda.synchronize()
+        print(json.dumps({'kernel': 'compare', 'shape': [m, n, k], 'launches': 3 * args.steps}), flush=True)
+        return
     elif args.kernel == 'readout':
         rows = torch.randn(n, k, generator=g, device=dev) * 0.02
         hl = x[:m]
@@ -743,7 +761,8 @@ def main():
     ap.add_argument('--cpu-seconds', type=float, default=10.0)
     ap.add_argument('--shape', default=None,
                     help='M,N,K: time one kernel on one shape; sweep: the config-1 GEMMs once each (profiling)')
-    ap.add_argument('--kernel', default='gemm', help='gemm | swiglu | act_quant | rmsnorm_quant | qk_rope | readout')
+    ap.add_argument('--kernel', default='gemm',
+                    help='gemm | swiglu | act_quant | rmsnorm_quant | qk_rope | readout | compare')
     ap.add_argument('--tile', type=int, default=0, help='block_m*1000+block_n, 0 = library choice')
     ap.add_argument('--skip-model', action='store_true', help='only the config-1 GEMM sweep')
     args = ap.parse_args()
