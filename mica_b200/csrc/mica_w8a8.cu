@@ -152,6 +152,11 @@ static int gemm_launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUten
     return launch_status();
 }
 
+// Epilogue warps of the dequant GEMM per tile width. The 320-wide tile runs one tile per CTA, so
+// nothing hides its epilogue: eight warps (two per tensor-memory lane quarter) halve it.
+template <int BN>
+struct DequantWarps { static constexpr int EW = BN == 320 ? 8 : 4; };
+
 // ---- CTA-pair kernels ---------------------------------------------------------------------
 // Co-resident clusters of two per device (pairs of SMs the scheduler can place together).
 static std::atomic<int> g_pair_clusters[kMaxDev];
@@ -489,8 +494,8 @@ int mica_preload(int* n_kernels) {
     int rc = check_device(nullptr);
     if (rc) return rc;
     int n = 0;
-#define PREP(BN, EPI, T)                                  \
-    if ((rc = gemm_prepare<BN, EPI, T>()) != MICA_OK) return rc; \
+#define PREP(BN, EPI, T)                                                            \
+    if ((rc = gemm_prepare<BN, EPI, T, DequantWarps<BN>::EW>()) != MICA_OK) return rc; \
     ++n;
     PREP(64, EPI_DEQUANT, __nv_bfloat16)
     PREP(128, EPI_DEQUANT, __nv_bfloat16)
@@ -670,9 +675,10 @@ static int gemm_checks(const int8_t* A, long lda, const int8_t* B, long ldb, con
 template <int BN>
 static int gemm_dispatch_out(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const GemmArgs& g,
                              int c_dtype, int grid, cudaStream_t st) {
-    if (c_dtype == MICA_DT_BF16) return gemm_launch<BN, EPI_DEQUANT, __nv_bfloat16>(ta, tb, tc, g, grid, false, st);
-    if (c_dtype == MICA_DT_FP16) return gemm_launch<BN, EPI_DEQUANT, __half>(ta, tb, tc, g, grid, false, st);
-    return gemm_launch<BN, EPI_DEQUANT, float>(ta, tb, tc, g, grid, false, st);
+    constexpr int EW = DequantWarps<BN>::EW;
+    if (c_dtype == MICA_DT_BF16) return gemm_launch<BN, EPI_DEQUANT, __nv_bfloat16, EW>(ta, tb, tc, g, grid, false, st);
+    if (c_dtype == MICA_DT_FP16) return gemm_launch<BN, EPI_DEQUANT, __half, EW>(ta, tb, tc, g, grid, false, st);
+    return gemm_launch<BN, EPI_DEQUANT, float, EW>(ta, tb, tc, g, grid, false, st);
 }
 
 size_t mica_w8a8_gemm_workspace_bytes(int M, int N, int K, int block_m, int block_n, int max_ctas, int splits) {
