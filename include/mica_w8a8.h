@@ -277,6 +277,18 @@ int mica_option_logits(const void* h, int h_dtype, long ldh,
 int mica_qk_norm_rope(void* qkv, long ld, const void* q_w, const void* k_w, const void* cos, const void* sin,
                       const int64_t* pos, long pos0, int S, int H, int KV, int D, float eps, void* stream);
 
+/* Causal grouped-query attention forward of the prefill on tcgen05 tensor cores, reading Q, K
+ * and V in place from the QKV projection's output:
+ *   qkv [B * L, >= (H + 2 KV) * D] bf16, row stride ld_qkv elements: per row q (H heads of D),
+ *       then k (KV heads), then v (KV heads); rows b * L .. b * L + L - 1 are request b;
+ *   out [B * L, >= H * D] bf16, row stride ld_out: out[t, h] = sum over keys s <= t of request
+ *       b of softmax_s(scale * q[t, h] . k[s, h / (H / KV)]) v[s, h / (H / KV)].
+ * fp32 scores and accumulation. D == 128, H % KV == 0. Replaces the torch SDPA call of the
+ * reference's prefill (v0.5/serving/lib/prefill_engine.py:308-324, lib/fast_runtime.py:189-220;
+ * the reference's own Triton kernel is v0.5/serving/kernel_src/kernels.py:72-124).           */
+int mica_attention_prefill(const void* qkv, long ld_qkv, void* out, long ld_out, int B, int L, int H, int KV, int D,
+                           float scale, void* stream);
+
 /* Failure-detection self-test: launches one block that waits on a barrier nothing
  * ever arrives on, with a wait limit of limit_us microseconds. The kernel gives up,
  * records MICA_DEV_TIMEOUT_SELFTEST in *status_dev (device int) and returns; the GPU

@@ -87,6 +87,7 @@ SIGNATURES = {
     'mica_swiglu_quant': (_I, [_P, _L, _P, _L, _I, _P, _P, _L, _P, _L, _P, _I, _I, _I, _P]),
     'mica_option_logits': (_I, [_P, _I, _L, _P, _I, _F, _P, _I, _I, _P, _P, _P, _P, _I, _P]),
     'mica_qk_norm_rope': (_I, [_P, _L, _P, _P, _P, _P, _P, _L, _I, _I, _I, _I, _F, _P]),
+    'mica_attention_prefill': (_I, [_P, _L, _P, _L, _I, _I, _I, _I, _I, _F, _P]),
     'mica_selftest_wait_timeout': (_I, [_P, _I, _P]),
 }
 

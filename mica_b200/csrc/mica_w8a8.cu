@@ -21,6 +21,7 @@
 #include "quant.cuh"
 #include "readout.cuh"
 #include "qk_rope.cuh"
+#include "attention.cuh"
 
 using namespace mica;
 
@@ -987,6 +988,46 @@ int mica_qk_norm_rope(void* qkv, long ld, const void* q_w, const void* k_w, cons
         const unsigned blocks = static_cast<unsigned>((warps * 32 + 255) / 256);
         qk_norm_rope_kernel<64><<<blocks, 256, 0, st>>>(a);
     }
+    return launch_status();
+}
+
+// ---------------------------------------------------------------------------------------
+int mica_attention_prefill(const void* qkv, long ld_qkv, void* out, long ld_out, int B, int L, int H, int KV, int D,
+                           float scale, void* stream) {
+    if (!qkv || !out || !(scale > 0.f)) return MICA_ERR_ARG;
+    if (B < 0 || L < 0 || H < 1 || KV < 1 || H % KV || D != ATT_D || ld_qkv < static_cast<long>(H + 2 * KV) * D ||
+        ld_out < static_cast<long>(H) * D)
+        return MICA_ERR_SHAPE;
+    if (!aligned16(qkv) || !aligned16(out) || (ld_qkv * 2) % 16 || (ld_out * 2) % 16) return MICA_ERR_ALIGN;
+    const long rows = static_cast<long>(B) * L;
+    const long ctas = static_cast<long>(B) * ((L + ATT_BM - 1) / ATT_BM) * H;
+    if (rows > (1L << 31) - 1 || ctas > (1L << 31) - 1) return MICA_ERR_RANGE;
+    int rc = check_device(nullptr);
+    if (rc) return rc;
+    if (rows == 0) return MICA_OK;
+    {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        static std::atomic<uint64_t> done{0};
+        const uint64_t bit = 1ull << (dev & 63);
+        if (!(done.load(std::memory_order_acquire) & bit)) {
+            cudaError_t e = cudaFuncSetAttribute(attention_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 ATT_SMEM_BYTES);
+            if (e != cudaSuccess) { set_cuda_error(e); return MICA_ERR_CUDA; }
+            done.fetch_or(bit, std::memory_order_release);
+        }
+    }
+    CUtensorMap tm;
+    if ((rc = make_tmap_2d(&tm, qkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, static_cast<uint64_t>(H + 2 * KV) * D,
+                           static_cast<uint64_t>(rows), static_cast<uint64_t>(ld_qkv) * 2, 64, ATT_BM)))
+        return rc;
+    AttnArgs a = {};
+    a.qkv = static_cast<const __nv_bfloat16*>(qkv); a.ld_qkv = ld_qkv;
+    a.out = static_cast<__nv_bfloat16*>(out); a.ld_out = ld_out;
+    a.B = B; a.L = L; a.H = H; a.KV = KV;
+    a.scale_log2 = scale * 1.4426950408889634f;
+    attention_fwd_kernel<<<static_cast<unsigned>(ctas), ATT_THREADS, ATT_SMEM_BYTES, static_cast<cudaStream_t>(stream)>>>(
+        tm, a);
     return launch_status();
 }
 

@@ -15,6 +15,7 @@ shapes without running anything.
     torch.ops.mica.swiglu_quant(g, u, inv, round_mode, want_h, want_q) -> (h, q, s)
     torch.ops.mica.option_logits(h, rows, gamma, lo, hi, eps, style)    -> (logits, probs)
     torch.ops.mica.qk_norm_rope(qkv, q_w, k_w, cos, sin, pos, pos0, heads, kv_heads, eps)  (in place)
+    torch.ops.mica.attention_prefill(qkv, B, L, heads, kv_heads, scale)  -> o [B * L, heads * D]
 """
 from __future__ import annotations
 
@@ -258,3 +259,22 @@ def qk_norm_rope(qkv: torch.Tensor, q_w: Optional[torch.Tensor], k_w: Optional[t
 @qk_norm_rope.register_fake
 def _(qkv, q_w, k_w, cos, sin, pos, pos0, heads, kv_heads, eps):
     return None
+
+
+# ---------------------------------------------------------------------------------------
+@torch.library.custom_op('mica::attention_prefill', mutates_args=())
+def attention_prefill(qkv: torch.Tensor, batch: int, length: int, heads: int, kv_heads: int,
+                      scale: float) -> torch.Tensor:
+    """Causal GQA attention of a [batch, length] prefill on the QKV projection output (D = 128)."""
+    d = qkv.shape[1] // (heads + 2 * kv_heads)
+    out = torch.empty((qkv.shape[0], heads * d), dtype=torch.bfloat16, device=qkv.device)
+    with _on(qkv):
+        N.call('mica_attention_prefill', qkv.data_ptr(), qkv.stride(0), out.data_ptr(), out.stride(0), batch, length,
+               heads, kv_heads, d, scale, _stream(qkv))
+    return out
+
+
+@attention_prefill.register_fake
+def _(qkv, batch, length, heads, kv_heads, scale):
+    d = qkv.shape[1] // (heads + 2 * kv_heads)
+    return qkv.new_empty((qkv.shape[0], heads * d))
