@@ -667,11 +667,12 @@ def run_shape(args):
         return
     m, n, k = (int(v) for v in args.shape.split(','))
     g = torch.Generator(device=dev).manual_seed(7)
-    x = torch.randn(m, k, generator=g, device=dev).to(torch.bfloat16)
-    w = torch.randint(-127, 128, (n, k), generator=g, device=dev, dtype=torch.int8)
-    sw = torch.rand(n, generator=g, device=dev) * 9e-3 + 1e-3
-    q, s = torch.ops.mica.act_quant(x, None, 0)
-    gamma = (1 + 0.1 * torch.randn(k, generator=g, device=dev)).to(torch.bfloat16)
+    if args.kernel != 'attention':
+        x = torch.randn(m, k, generator=g, device=dev).to(torch.bfloat16)
+        w = torch.randint(-127, 128, (n, k), generator=g, device=dev, dtype=torch.int8)
+        sw = torch.rand(n, generator=g, device=dev) * 9e-3 + 1e-3
+        q, s = torch.ops.mica.act_quant(x, None, 0)
+        gamma = (1 + 0.1 * torch.randn(k, generator=g, device=dev)).to(torch.bfloat16)
     if args.kernel == 'gemm':
         fn, work = (lambda: torch.ops.mica.w8a8_gemm(q, s, w, sw, None, 0, args.tile)), ('TOPS', 2 * m * n * k)
     elif args.kernel == 'swiglu':
@@ -691,6 +692,12 @@ def run_shape(args):
         qw = gamma[:128].contiguous()
         fn = lambda: torch.ops.mica.qk_norm_rope(qkv, qw, qw, cos, sin, None, 0, 32, 8, 1e-6)  # noqa: E731
         work = ('GB/s', m * 5120 * 2 * 2)
+    elif args.kernel == 'attention':
+        # --shape L,H,KV: one request of L tokens, H query / KV key-value heads of 128
+        L, H, KV = m, n, k
+        qkv = torch.randn(L, (H + 2 * KV) * 128, generator=g, device=dev).to(torch.bfloat16)
+        fn = lambda: torch.ops.mica.attention_prefill(qkv, 1, L, H, KV, 128 ** -0.5)  # noqa: E731
+        work = ('TFLOP/s', 4 * H * 128 * L * (L + 1) // 2)
     elif args.kernel == 'compare':
         # cuBLASLt's int8 GEMM (torch._int_mm, int32 out) beside this library's 128 x 256 and CTA-pair
         # GEMMs on the same operands, once per step each; the timed steps run inside the NVTX range
@@ -726,7 +733,7 @@ def run_shape(args):
     torch.cuda.synchronize()
     ms = a.elapsed_time(b) / args.steps
     unit, amount = work
-    rate = amount / ms / 1e9 if unit == 'TOPS' else amount / ms / 1e6
+    rate = amount / ms / 1e9 if unit in ('TOPS', 'TFLOP/s') else amount / ms / 1e6
     print(json.dumps({'kernel': args.kernel, 'shape': [m, n, k], 'tile': args.tile, 'ms_per_launch': round(ms, 4),
                       unit: round(rate, 1)}), flush=True)
 
@@ -762,7 +769,8 @@ def main():
     ap.add_argument('--shape', default=None,
                     help='M,N,K: time one kernel on one shape; sweep: the config-1 GEMMs once each (profiling)')
     ap.add_argument('--kernel', default='gemm',
-                    help='gemm | swiglu | act_quant | rmsnorm_quant | qk_rope | readout | compare')
+                    help='gemm | swiglu | act_quant | rmsnorm_quant | qk_rope | readout | compare | attention '
+                         '(--shape L,H,KV)')
     ap.add_argument('--tile', type=int, default=0, help='block_m*1000+block_n, 0 = library choice')
     ap.add_argument('--skip-model', action='store_true', help='only the config-1 GEMM sweep')
     args = ap.parse_args()

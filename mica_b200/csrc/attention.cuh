@@ -6,20 +6,24 @@
 // columns), D = 128, G = H / KV query heads per key/value head; each request of a [B, L] batch
 // attends within its own L rows. fp32 scores and accumulator, bf16 output [rows, H D].
 //
-// One CTA per (request, block of 128 query rows, query head), heaviest blocks first. Warps:
-//   warp 0      TMA producer: the Q tile once (two 64-column boxes, 128-byte swizzle), then
-//               K and V tiles of 128 keys in two rings of KV_STAGES stages;
-//   warp 1      one lane issues the MMAs: S_j = Q K_j^T (kind::f16, M 128, N 128, K 16 steps,
-//               both operands K-major in shared memory) into one of two TMEM score buffers,
-//               then O += P_{j-1} V_{j-1} with P read from tensor memory (the TS form) and V
-//               MN-major in shared memory, so scoring tile j overlaps the softmax of tile j-1;
-//   warps 2..5  softmax, one query row per thread: scores from TMEM, causal mask on the
-//               diagonal tile, running max in the exp2 domain, p = 2^(s c - m), row sum, P to
-//               TMEM as bf16 pairs. O is rescaled (read, scaled, written back in TMEM) only when
-//               the running max grows by more than 8 (a factor of 256): otherwise the stale max
-//               is kept, p stays below 2^8 and nothing is lost in fp32. At the end each thread
-//               divides its O row by its sum and stores it.
-// Tensor memory (512 columns): S0 [0,128) S1 [128,256) O [256,384) P0 [384,448) P1 [448,512).
+// One CTA per (request, block of 256 query rows, query head), heaviest blocks first: two query
+// tiles A and B of 128 rows share every K and V tile. Warps:
+//   warp 0      TMA producer: both Q tiles once (64-column boxes, 128-byte swizzle), then K and
+//               V tiles of 128 keys in rings of 3 and 2 stages;
+//   warp 1      one lane issues the MMAs: S = Q_X K_j^T (kind::f16, M 128, N 128, K 16 steps,
+//               both operands K-major in shared memory) and O_X += P_X V_j with P read from tensor
+//               memory (the TS form) and V MN-major in shared memory;
+//   warps 2..5  softmax of tile A, warps 6..9 of tile B, one query row per thread: scores from
+//               TMEM, causal mask on the diagonal tile, running max in the exp2 domain,
+//               p = 2^(s c - m), row sum, P to TMEM as bf16 pairs. O is rescaled in TMEM only when
+//               the running max grows by more than 8 (a factor of 256): otherwise the stale max is
+//               kept, p stays below 2^8 and nothing is lost in fp32. At the end each thread divides
+//               its O row by its sum and stores it.
+// Tensor memory (512 columns): S [0,128) P_A [128,192) P_B [192,256) O_A [256,384) O_B [384,512).
+// The one score buffer is taken in turn, S_A(0) S_B(0) S_A(1) S_B(1) ...: a tile's softmax frees it
+// as soon as it has the scores in registers, so the tensor core computes the other tile's scores
+// (and a P.V) while that softmax runs; the next P.V of a tile is issued when its P is written. MMA
+// order per key tile j: S_A(j+1), O_A += P_A(j) V_j, S_B(j+1), O_B += P_B(j) V_j.
 // Every wait is bounded (common.cuh); a wait that runs out unwinds the CTA.
 //
 // Reference semantics: the reference's prefill runs attention through torch SDPA
@@ -41,13 +45,16 @@ struct AttnArgs {
 };
 
 constexpr int ATT_D = 128;
-constexpr int ATT_BM = 128;                 // query rows per CTA
+constexpr int ATT_BM = 128;                 // query rows per tile (two tiles per CTA)
 constexpr int ATT_BN = 128;                 // keys per tile
 constexpr int ATT_HALF_BYTES = 128 * 128;   // one 128-row x 64-column bf16 box (128-byte rows)
 constexpr int ATT_TILE_BYTES = 2 * ATT_HALF_BYTES;
-constexpr int ATT_KV_STAGES = 3;
-constexpr int ATT_SMEM_BYTES = 1024 + ATT_TILE_BYTES * (1 + 2 * ATT_KV_STAGES) + 256;
-constexpr int ATT_THREADS = 192;
+// K is needed one step ahead of V (the next scores are issued right after this step's P.V), so its
+// ring is a stage deeper: with two stages the TMA round trip of K_{j+1} sat on the critical path.
+constexpr int ATT_K_STAGES = 3;
+constexpr int ATT_V_STAGES = 2;
+constexpr int ATT_SMEM_BYTES = 1024 + ATT_TILE_BYTES * (2 + ATT_K_STAGES + ATT_V_STAGES) + 256;
+constexpr int ATT_THREADS = 320;
 constexpr float ATT_RESCALE_LOG2 = 8.0f;
 
 // kind::f16 instruction descriptor: fp32 accumulator, bf16 A and B, M 128, N 128; B K-major
@@ -91,6 +98,29 @@ __device__ __forceinline__ void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, ui
         : "memory");
 }
 
+__device__ __forceinline__ float fmax3(float a, float b, float d) {
+    float r;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(d));
+    return r;
+}
+__device__ __forceinline__ unsigned long long f2_fma(unsigned long long a, unsigned long long b, unsigned long long d) {
+    unsigned long long r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(d));
+    return r;
+}
+
+// 2^x0 and 2^x1 with one MUFU operation: the exponents rounded to an f16 pair (for the
+// x <= 8 that occur here, within 2^-12 relative: p moves by at most ~0.3 % where it matters,
+// x >= -16, below the bf16 rounding P gets for the second MMA), ex2.approx.f16x2, widened back.
+// Exponents below the f16 range (x < -24) give 0, as their p are below 2^-24.
+__device__ __forceinline__ void exp2_pair(float x0, float x1, float& p0, float& p1) {
+    uint32_t h, e;
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(x1), "f"(x0));
+    asm("ex2.approx.f16x2 %0, %1;" : "=r"(e) : "r"(h));
+    asm("{\n\t.reg .f16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\tcvt.f32.f16 %0, lo;\n\tcvt.f32.f16 %1, hi;\n\t}"
+        : "=f"(p0), "=f"(p1) : "r"(e));
+}
+
 __device__ __forceinline__ float fast_exp2(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -107,51 +137,54 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
 attention_fwd_kernel(const __grid_constant__ CUtensorMap tmap_qkv, const AttnArgs args) {
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int q_blocks = (args.L + ATT_BM - 1) / ATT_BM;
-    // heaviest (latest) query blocks first; within a block index, requests then heads
-    const int per_qb = args.B * args.H;
-    const int qb = q_blocks - 1 - static_cast<int>(blockIdx.x) / per_qb;
-    const int rem = static_cast<int>(blockIdx.x) % per_qb;
+    const int pairs = (args.L + 2 * ATT_BM - 1) / (2 * ATT_BM);
+    // heaviest (latest) blocks first; within a block index, requests then heads
+    const int per_cb = args.B * args.H;
+    const int cb = pairs - 1 - static_cast<int>(blockIdx.x) / per_cb;
+    const int rem = static_cast<int>(blockIdx.x) % per_cb;
     const int b = rem / args.H;
     const int h = rem % args.H;
     const int kvh = h / (args.H / args.KV);
-    const int q0 = qb * ATT_BM;
+    const int q0 = cb * 2 * ATT_BM;           // tile A rows q0.., tile B rows q0 + 128..
     const int row0 = b * args.L;              // first row of this request
-    const int nkv = att_key_tiles(qb, args.L);
+    const int nkv_a = att_key_tiles(2 * cb, args.L);
+    const int nkv_b = att_key_tiles(2 * cb + 1, args.L);   // >= nkv_a: the key tiles loaded
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-    uint8_t* sq = smem;
-    uint8_t* sk = smem + ATT_TILE_BYTES;
-    uint8_t* sv = sk + ATT_KV_STAGES * ATT_TILE_BYTES;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sv + ATT_KV_STAGES * ATT_TILE_BYTES);
+    uint8_t* sq = smem;                                       // Q_A, Q_B
+    uint8_t* sk = smem + 2 * ATT_TILE_BYTES;
+    uint8_t* sv = sk + ATT_K_STAGES * ATT_TILE_BYTES;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sv + ATT_V_STAGES * ATT_TILE_BYTES);
     uint64_t* q_full = bars;
     uint64_t* k_full = bars + 1;
-    uint64_t* k_empty = k_full + ATT_KV_STAGES;
-    uint64_t* v_full = k_empty + ATT_KV_STAGES;
-    uint64_t* v_empty = v_full + ATT_KV_STAGES;
-    uint64_t* s_full = v_empty + ATT_KV_STAGES;     // [2] MMA -> softmax: scores ready
-    uint64_t* s_read = s_full + 2;                  // [2] softmax -> MMA: scores read
-    uint64_t* p_full = s_read + 2;                  // [2] softmax -> MMA: P (and O rescale) written
-    uint64_t* p_done = p_full + 2;                  // [2] MMA -> softmax: P.V of that buffer finished
-    uint64_t* drain = p_done + 2;
+    uint64_t* k_empty = k_full + ATT_K_STAGES;
+    uint64_t* v_full = k_empty + ATT_K_STAGES;
+    uint64_t* v_empty = v_full + ATT_V_STAGES;
+    uint64_t* s_full = v_empty + ATT_V_STAGES;      // [2] per tile, MMA -> softmax: its scores are in S
+    uint64_t* s_free = s_full + 2;                  // softmax -> MMA: S read into registers (4 warps)
+    uint64_t* p_full = s_free + 1;                  // [2] softmax -> MMA: P (and any O rescale) written
+    uint64_t* pv_done = p_full + 2;                 // [2] MMA -> softmax: the tile's P.V finished
+    uint64_t* drain = pv_done + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
     volatile uint32_t* abort_flag = tmem_slot + 1;
 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
-        for (int i = 0; i < ATT_KV_STAGES; ++i) {
+        for (int i = 0; i < ATT_K_STAGES; ++i) {
             mbar_init(&k_full[i], 1);
             mbar_init(&k_empty[i], 1);
+        }
+        for (int i = 0; i < ATT_V_STAGES; ++i) {
             mbar_init(&v_full[i], 1);
             mbar_init(&v_empty[i], 1);
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&s_full[i], 1);
-            mbar_init(&s_read[i], 4);
             mbar_init(&p_full[i], 4);
-            mbar_init(&p_done[i], 1);
+            mbar_init(&pv_done[i], 1);
         }
+        mbar_init(s_free, 4);
         mbar_init(drain, 1);
         *abort_flag = 0u;
         fence_mbar_init();
@@ -162,7 +195,6 @@ attention_fwd_kernel(const __grid_constant__ CUtensorMap tmap_qkv, const AttnArg
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const uint32_t t_s = tmem, t_o = tmem + 256, t_p = tmem + 384;
 
     const int qcol = h * ATT_D;
     const int kcol = (args.H + kvh) * ATT_D;
@@ -172,32 +204,46 @@ attention_fwd_kernel(const __grid_constant__ CUtensorMap tmap_qkv, const AttnArg
         // ---------------------------------- producer ----------------------------------
         if (lane == 0) {
             const uint64_t pol_kv = policy_evict_last();     // re-read by the G query heads and later blocks
-            mbar_arrive_expect_tx(q_full, ATT_TILE_BYTES);
-            tma_load_2d(sq, &tmap_qkv, q_full, qcol, row0 + q0);
-            tma_load_2d(sq + ATT_HALF_BYTES, &tmap_qkv, q_full, qcol + 64, row0 + q0);
+            mbar_arrive_expect_tx(q_full, 2 * ATT_TILE_BYTES);
+            for (int t = 0; t < 2; ++t) {
+                tma_load_2d(sq + t * ATT_TILE_BYTES, &tmap_qkv, q_full, qcol, row0 + q0 + t * ATT_BM);
+                tma_load_2d(sq + t * ATT_TILE_BYTES + ATT_HALF_BYTES, &tmap_qkv, q_full, qcol + 64,
+                            row0 + q0 + t * ATT_BM);
+            }
             bool ok = true;
-            for (int j = 0; j < nkv && ok; ++j) {
-                const int st = j % ATT_KV_STAGES;
-                const uint32_t ph = (j / ATT_KV_STAGES) & 1u;
-                const int k0 = row0 + j * ATT_BN;
-                if (!mbar_wait(&k_empty[st], ph ^ 1u, abort_flag, MICA_DEV_TIMEOUT_PRODUCER)) { ok = false; break; }
+            // K runs up to ATT_K_STAGES tiles ahead, V up to ATT_V_STAGES: load K_j, then V_{j-d}
+            // where d = ATT_K_STAGES - ATT_V_STAGES, so a full V ring never holds back K
+            constexpr int d = ATT_K_STAGES - ATT_V_STAGES;
+            auto load_k = [&](int j) {
+                const int st = j % ATT_K_STAGES;
+                if (!mbar_wait(&k_empty[st], ((j / ATT_K_STAGES) & 1u) ^ 1u, abort_flag, MICA_DEV_TIMEOUT_PRODUCER))
+                    return false;
                 mbar_arrive_expect_tx(&k_full[st], ATT_TILE_BYTES);
                 uint8_t* kd = sk + st * ATT_TILE_BYTES;
-                tma_load_2d_hint(kd, &tmap_qkv, &k_full[st], kcol, k0, pol_kv);
-                tma_load_2d_hint(kd + ATT_HALF_BYTES, &tmap_qkv, &k_full[st], kcol + 64, k0, pol_kv);
-                if (!mbar_wait(&v_empty[st], ph ^ 1u, abort_flag, MICA_DEV_TIMEOUT_PRODUCER)) { ok = false; break; }
+                tma_load_2d_hint(kd, &tmap_qkv, &k_full[st], kcol, row0 + j * ATT_BN, pol_kv);
+                tma_load_2d_hint(kd + ATT_HALF_BYTES, &tmap_qkv, &k_full[st], kcol + 64, row0 + j * ATT_BN, pol_kv);
+                return true;
+            };
+            auto load_v = [&](int j) {
+                const int st = j % ATT_V_STAGES;
+                if (!mbar_wait(&v_empty[st], ((j / ATT_V_STAGES) & 1u) ^ 1u, abort_flag, MICA_DEV_TIMEOUT_PRODUCER))
+                    return false;
                 mbar_arrive_expect_tx(&v_full[st], ATT_TILE_BYTES);
                 uint8_t* vd = sv + st * ATT_TILE_BYTES;
-                tma_load_2d_hint(vd, &tmap_qkv, &v_full[st], vcol, k0, pol_kv);
-                tma_load_2d_hint(vd + ATT_HALF_BYTES, &tmap_qkv, &v_full[st], vcol + 64, k0, pol_kv);
+                tma_load_2d_hint(vd, &tmap_qkv, &v_full[st], vcol, row0 + j * ATT_BN, pol_kv);
+                tma_load_2d_hint(vd + ATT_HALF_BYTES, &tmap_qkv, &v_full[st], vcol + 64, row0 + j * ATT_BN, pol_kv);
+                return true;
+            };
+            for (int j = 0; j < nkv_b + d && ok; ++j) {
+                if (j < nkv_b && !load_k(j)) ok = false;
+                if (ok && j >= d && !load_v(j - d)) ok = false;
             }
             // the last loads of each ring land before shared memory is released
             mbar_wait(q_full, 0, abort_flag, MICA_DEV_TIMEOUT_DRAIN);
-            const int first = nkv > ATT_KV_STAGES ? nkv - ATT_KV_STAGES : 0;
-            for (int j = first; j < nkv && ok; ++j) {
-                mbar_wait(&k_full[j % ATT_KV_STAGES], (j / ATT_KV_STAGES) & 1u, abort_flag, MICA_DEV_TIMEOUT_DRAIN);
-                mbar_wait(&v_full[j % ATT_KV_STAGES], (j / ATT_KV_STAGES) & 1u, abort_flag, MICA_DEV_TIMEOUT_DRAIN);
-            }
+            for (int j = nkv_b > ATT_K_STAGES ? nkv_b - ATT_K_STAGES : 0; j < nkv_b && ok; ++j)
+                mbar_wait(&k_full[j % ATT_K_STAGES], (j / ATT_K_STAGES) & 1u, abort_flag, MICA_DEV_TIMEOUT_DRAIN);
+            for (int j = nkv_b > ATT_V_STAGES ? nkv_b - ATT_V_STAGES : 0; j < nkv_b && ok; ++j)
+                mbar_wait(&v_full[j % ATT_V_STAGES], (j / ATT_V_STAGES) & 1u, abort_flag, MICA_DEV_TIMEOUT_DRAIN);
         }
         __syncwarp();
     } else if (warp == 1) {
@@ -205,47 +251,63 @@ attention_fwd_kernel(const __grid_constant__ CUtensorMap tmap_qkv, const AttnArg
         if (lane == 0) {
             constexpr uint32_t idesc_qk = idesc_bf16(ATT_BM, ATT_BN, false);
             constexpr uint32_t idesc_pv = idesc_bf16(ATT_BM, ATT_D, true);
-            const uint32_t q_addr = smem_u32(sq);
+            const int nkv[2] = {nkv_a, nkv_b};
             bool ok = mbar_wait(q_full, 0, abort_flag, MICA_DEV_TIMEOUT_MMA);
-            // issue order: S0, S1, PV0, S2, PV1, ... so the scores of tile j+1 are computed
-            // while the softmax works on tile j
-            for (int step = 0; step <= nkv && ok; ++step) {
-                if (step < nkv) {
-                    const int j = step;
-                    const int sb = j & 1;
-                    const int st = j % ATT_KV_STAGES;
-                    if (!mbar_wait(&k_full[st], (j / ATT_KV_STAGES) & 1u, abort_flag, MICA_DEV_TIMEOUT_MMA)) break;
-                    // the softmax has read this score buffer's previous tile (j - 2)
-                    if (j >= 2 && !mbar_wait(&s_read[sb], ((j - 2) >> 1) & 1u, abort_flag, MICA_DEV_TIMEOUT_MMA))
-                        break;
-                    tc_fence_after();
-                    const uint32_t k_addr = smem_u32(sk + st * ATT_TILE_BYTES);
+            // S = Q_X K_j^T; the fills of S alternate between the tiles and each waits until the
+            // previous one has been read (s_free completes once per fill)
+            int fills = 0;
+            // descriptors of the stage bases; a byte offset within a tile adds (offset >> 4)
+            const uint64_t q_desc0 = smem_desc_sw128(smem_u32(sq), 16, 1024);
+            const uint64_t k_desc0 = smem_desc_sw128(smem_u32(sk), 16, 1024);
+            const uint64_t v_desc0 = smem_desc_sw128(smem_u32(sv), ATT_HALF_BYTES, 1024);
+            constexpr uint64_t kTileStep = ATT_TILE_BYTES >> 4;
+            auto scores = [&](int x, int j) {
+                if (fills > 0 && !mbar_wait(s_free, (fills - 1) & 1u, abort_flag, MICA_DEV_TIMEOUT_MMA)) return false;
+                tc_fence_after();
+                const uint64_t qd = q_desc0 + static_cast<uint64_t>(x) * kTileStep;
+                const uint64_t kd = k_desc0 + static_cast<uint64_t>(j % ATT_K_STAGES) * kTileStep;
 #pragma unroll
-                    for (int kk = 0; kk < ATT_D / 16; ++kk) {
-                        const uint32_t off = (kk >> 2) * ATT_HALF_BYTES + (kk & 3) * 32;
-                        mma_bf16_ss(t_s + sb * 128, smem_desc_sw128(q_addr + off, 16, 1024),
-                                    smem_desc_sw128(k_addr + off, 16, 1024), idesc_qk, kk > 0 ? 1u : 0u);
-                    }
-                    mma_commit(&k_empty[st]);
-                    mma_commit(&s_full[sb]);
+                for (int kk = 0; kk < ATT_D / 16; ++kk) {
+                    const uint64_t off = static_cast<uint64_t>(((kk >> 2) * ATT_HALF_BYTES + (kk & 3) * 32) >> 4);
+                    mma_bf16_ss(tmem, qd + off, kd + off, idesc_qk, kk > 0 ? 1u : 0u);
                 }
-                if (step >= 1) {
-                    const int j = step - 1;
-                    const int pb = j & 1;
-                    const int st = j % ATT_KV_STAGES;
-                    if (!mbar_wait(&p_full[pb], (j >> 1) & 1u, abort_flag, MICA_DEV_TIMEOUT_MMA)) break;
-                    if (!mbar_wait(&v_full[st], (j / ATT_KV_STAGES) & 1u, abort_flag, MICA_DEV_TIMEOUT_MMA)) break;
-                    tc_fence_after();
-                    const uint32_t v_addr = smem_u32(sv + st * ATT_TILE_BYTES);
+                mma_commit(&s_full[x]);
+                ++fills;
+                return true;
+            };
+            // O_X += P_X V_j once tile X's softmax has written P_X(j)
+            auto values = [&](int x, int j) {
+                if (!mbar_wait(&p_full[x], j & 1u, abort_flag, MICA_DEV_TIMEOUT_MMA)) return false;
+                tc_fence_after();
+                const uint64_t vd = v_desc0 + static_cast<uint64_t>(j % ATT_V_STAGES) * kTileStep;
+                const uint32_t d_o = tmem + 256 + x * 128, a_p = tmem + 128 + x * 64;
+                mma_bf16_ts(d_o, a_p, vd, idesc_pv, j > 0 ? 1u : 0u);
 #pragma unroll
-                    for (int kk = 0; kk < ATT_BN / 16; ++kk) {
-                        // 16 keys: 8 columns of P (bf16 pairs); V rows kk*16.. as the K of the MMA
-                        mma_bf16_ts(t_o, t_p + pb * 64 + kk * 8, smem_desc_sw128(v_addr + kk * 16 * 128, ATT_HALF_BYTES, 1024),
-                                    idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
-                    }
-                    mma_commit(&v_empty[st]);
-                    mma_commit(&p_done[pb]);
+                for (int kk = 1; kk < ATT_BN / 16; ++kk)
+                    mma_bf16_ts(d_o, a_p + kk * 8, vd + ((kk * 16 * 128) >> 4), idesc_pv, 1u);
+                mma_commit(&pv_done[x]);
+                return true;
+            };
+            auto k_ready = [&](int j) {
+                return mbar_wait(&k_full[j % ATT_K_STAGES], (j / ATT_K_STAGES) & 1u, abort_flag, MICA_DEV_TIMEOUT_MMA);
+            };
+            ok = ok && k_ready(0) && (nkv[0] == 0 || scores(0, 0)) && scores(1, 0);
+            if (ok) mma_commit(&k_empty[0]);
+            for (int j = 0; j < nkv_b && ok; ++j) {
+                const bool next = j + 1 < nkv_b;
+                if (next && !k_ready(j + 1)) { ok = false; break; }
+                if (j + 1 < nkv[0] && !scores(0, j + 1)) { ok = false; break; }
+                if (!mbar_wait(&v_full[j % ATT_V_STAGES], (j / ATT_V_STAGES) & 1u, abort_flag, MICA_DEV_TIMEOUT_MMA)) {
+                    ok = false;
+                    break;
                 }
+                if (j < nkv[0] && !values(0, j)) { ok = false; break; }
+                if (next) {
+                    if (!scores(1, j + 1)) { ok = false; break; }
+                    mma_commit(&k_empty[(j + 1) % ATT_K_STAGES]);   // both tiles' scores of K_{j+1} issued
+                }
+                if (!values(1, j)) { ok = false; break; }
+                mma_commit(&v_empty[j % ATT_V_STAGES]);             // both tiles' P.V of V_j issued
             }
             mma_commit(drain);
             mbar_wait(drain, 0, abort_flag, MICA_DEV_TIMEOUT_DRAIN);
@@ -253,93 +315,115 @@ attention_fwd_kernel(const __grid_constant__ CUtensorMap tmap_qkv, const AttnArg
         __syncwarp();
     } else {
         // ---------------------------------- softmax ----------------------------------
+        const int x = (warp - 2) >> 2;                    // query tile of this warpgroup
         const int q4 = warp & 3;
         const int r = q4 * 32 + lane;                     // row in the tile
-        const int qi = q0 + r;                            // query index in the request
+        const int qt0 = q0 + x * ATT_BM;                  // first query of the tile
+        const int qi = qt0 + r;                           // query index in the request
+        const int nkv = x == 0 ? nkv_a : nkv_b;
         const uint32_t lane_off = static_cast<uint32_t>(q4 * 32) << 16;
+        const uint32_t t_s = tmem + lane_off, t_p = tmem + 128 + x * 64 + lane_off;
+        const uint32_t t_o = tmem + 256 + x * 128 + lane_off;
         const float c = args.scale_log2;
         float m_use = -1e30f;                             // running max (exp2 domain) in use
         float l = 0.f;                                    // running sum of p
         bool ok = true;
         for (int j = 0; j < nkv; ++j) {
-            const int sb = j & 1;
             bool w = true;
-            if (lane == 0) w = mbar_wait(&s_full[sb], (j >> 1) & 1u, abort_flag, MICA_DEV_TIMEOUT_EPILOGUE);
+            if (lane == 0) w = mbar_wait(&s_full[x], j & 1u, abort_flag, MICA_DEV_TIMEOUT_EPILOGUE);
             if (!__shfl_sync(0xffffffffu, w, 0)) { ok = false; break; }
             tc_fence_after();
             uint32_t sr[128];
 #pragma unroll
             for (int cc = 0; cc < 4; ++cc) {
                 uint32_t (&part)[32] = *reinterpret_cast<uint32_t (*)[32]>(&sr[cc * 32]);
-                tmem_ld_32x32b_x32(t_s + sb * 128 + lane_off + cc * 32, part);
+                tmem_ld_32x32b_x32(t_s + cc * 32, part);
             }
             tmem_ld_wait();
+            // S goes back to the MMA issuer for the other tile's scores
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&s_read[sb]);
+            if (lane == 0) mbar_arrive(s_free);
             // causal and length mask on the tile that reaches the diagonal or the end
             const int k0 = j * ATT_BN;
-            const bool masked = k0 + ATT_BN - 1 > q0 || k0 + ATT_BN > args.L;
-            float mx = -INFINITY;
+            if (k0 + ATT_BN - 1 > qt0 || k0 + ATT_BN > args.L) {
 #pragma unroll
-            for (int i = 0; i < 128; ++i) {
-                float s = __uint_as_float(sr[i]) * c;
-                if (masked && (k0 + i > qi || k0 + i >= args.L)) s = -INFINITY;
-                sr[i] = __float_as_uint(s);
-                mx = fmaxf(mx, s);
+                for (int i = 0; i < 128; ++i)
+                    if (k0 + i > qi || k0 + i >= args.L) sr[i] = __float_as_uint(-INFINITY);
             }
+            // row max: eight independent chains of three-input max
+            float mp[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) mp[e] = fmax3(__uint_as_float(sr[e]), __uint_as_float(sr[8 + e]),
+                                                    __uint_as_float(sr[16 + e]));
+#pragma unroll
+            for (int i = 24; i < 128; i += 16) {
+#pragma unroll
+                for (int e = 0; e < 8; ++e)
+                    mp[e] = fmax3(mp[e], __uint_as_float(sr[i + e]), __uint_as_float(sr[i + 8 + e]));
+            }
+            const float mx = fmax3(fmax3(mp[0], mp[1], mp[2]), fmax3(mp[3], mp[4], mp[5]), fmaxf(mp[6], mp[7])) * c;
             float alpha = 1.f;
             const bool rescale = mx > m_use + ATT_RESCALE_LOG2;
             if (rescale) {
                 alpha = fast_exp2(m_use - mx);
                 m_use = mx;
             }
-            float sum = 0.f;
+            // p = 2^(s c - m): one f32x2 fma per two scores, one paired exp2, one f32x2 add into
+            // four partial sums, one bf16x2 pack
+            const unsigned long long c2 = f2_pack(c, c);
+            const unsigned long long nm2 = f2_pack(-m_use, -m_use);
+            unsigned long long sp[4] = {0ull, 0ull, 0ull, 0ull};
             uint32_t pk[64];
 #pragma unroll
             for (int i = 0; i < 64; ++i) {
-                const float p0 = fast_exp2(__uint_as_float(sr[2 * i]) - m_use);
-                const float p1 = fast_exp2(__uint_as_float(sr[2 * i + 1]) - m_use);
-                sum += p0 + p1;
+                const unsigned long long x2 = f2_fma(f2_pack(__uint_as_float(sr[2 * i]), __uint_as_float(sr[2 * i + 1])),
+                                                     c2, nm2);
+                float x0, x1;
+                f2_unpack(x2, x0, x1);
+                float p0, p1;
+                exp2_pair(x0, x1, p0, p1);
+                sp[i & 3] = f2_add(sp[i & 3], f2_pack(p0, p1));
                 pk[i] = pack_bf16(p0, p1);
             }
-            l = l * alpha + sum;
-            // O must hold P_{j-1} V_{j-1} before it is rescaled, and P_{j-2} V_{j-2} must be done
-            // with this P buffer before it is overwritten
-            if (j >= 1 && rescale) {
-                if (lane == 0) w = mbar_wait(&p_done[(j - 1) & 1], ((j - 1) >> 1) & 1u, abort_flag, MICA_DEV_TIMEOUT_EPILOGUE);
+            float a0, a1, b0, b1, d0, d1, e0, e1;
+            f2_unpack(sp[0], a0, a1);
+            f2_unpack(sp[1], b0, b1);
+            f2_unpack(sp[2], d0, d1);
+            f2_unpack(sp[3], e0, e1);
+            l = l * alpha + (((a0 + a1) + (b0 + b1)) + ((d0 + d1) + (e0 + e1)));
+            // P_X and O_X are free again once the previous P.V is done
+            if (j >= 1) {
+                if (lane == 0) w = mbar_wait(&pv_done[x], (j - 1) & 1u, abort_flag, MICA_DEV_TIMEOUT_EPILOGUE);
                 if (!__shfl_sync(0xffffffffu, w, 0)) { ok = false; break; }
                 tc_fence_after();
+            }
+            if (j >= 1 && rescale) {
 #pragma unroll
                 for (int cc = 0; cc < 4; ++cc) {
                     uint32_t o[32];
-                    tmem_ld_32x32b_x32(t_o + lane_off + cc * 32, o);
+                    tmem_ld_32x32b_x32(t_o + cc * 32, o);
                     tmem_ld_wait();
 #pragma unroll
                     for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-                    tmem_st_32x32b_x32(t_o + lane_off + cc * 32, o);
+                    tmem_st_32x32b_x32(t_o + cc * 32, o);
                 }
-            }
-            if (j >= 2) {
-                if (lane == 0) w = mbar_wait(&p_done[sb], ((j - 2) >> 1) & 1u, abort_flag, MICA_DEV_TIMEOUT_EPILOGUE);
-                if (!__shfl_sync(0xffffffffu, w, 0)) { ok = false; break; }
-                tc_fence_after();
             }
 #pragma unroll
             for (int half = 0; half < 2; ++half) {
                 uint32_t (&part)[32] = *reinterpret_cast<uint32_t (*)[32]>(&pk[half * 32]);
-                tmem_st_32x32b_x32(t_p + sb * 64 + lane_off + half * 32, part);
+                tmem_st_32x32b_x32(t_p + half * 32, part);
             }
             tmem_st_wait();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&p_full[sb]);
+            if (lane == 0) mbar_arrive(&p_full[x]);
         }
-        if (ok) {
-            // the last P.V is done: normalise and store this thread's output row
+        if (ok && nkv > 0) {
+            // the tile's last P.V is done: normalise and store this thread's output row
             const int jl = nkv - 1;
             bool w = true;
-            if (lane == 0) w = mbar_wait(&p_done[jl & 1], (jl >> 1) & 1u, abort_flag, MICA_DEV_TIMEOUT_EPILOGUE);
+            if (lane == 0) w = mbar_wait(&pv_done[x], jl & 1u, abort_flag, MICA_DEV_TIMEOUT_EPILOGUE);
             if (__shfl_sync(0xffffffffu, w, 0)) {
                 tc_fence_after();
                 const float inv = 1.f / l;
@@ -347,7 +431,7 @@ attention_fwd_kernel(const __grid_constant__ CUtensorMap tmap_qkv, const AttnArg
 #pragma unroll
                 for (int cc = 0; cc < 4; ++cc) {
                     uint32_t o[32];
-                    tmem_ld_32x32b_x32(t_o + lane_off + cc * 32, o);
+                    tmem_ld_32x32b_x32(t_o + cc * 32, o);
                     tmem_ld_wait();
                     if (qi < args.L) {
 #pragma unroll

@@ -1000,7 +1000,7 @@ int mica_attention_prefill(const void* qkv, long ld_qkv, void* out, long ld_out,
         return MICA_ERR_SHAPE;
     if (!aligned16(qkv) || !aligned16(out) || (ld_qkv * 2) % 16 || (ld_out * 2) % 16) return MICA_ERR_ALIGN;
     const long rows = static_cast<long>(B) * L;
-    const long ctas = static_cast<long>(B) * ((L + ATT_BM - 1) / ATT_BM) * H;
+    const long ctas = static_cast<long>(B) * ((L + 2 * ATT_BM - 1) / (2 * ATT_BM)) * H;
     if (rows > (1L << 31) - 1 || ctas > (1L << 31) - 1) return MICA_ERR_RANGE;
     int rc = check_device(nullptr);
     if (rc) return rc;
