@@ -59,6 +59,23 @@ constexpr float ATT_RESCALE_LOG2 = 8.0f;
 
 // kind::f16 instruction descriptor: fp32 accumulator, bf16 A and B, M 128, N 128; B K-major
 // (scores) or MN-major (the value tile, d contiguous).
+// Bounded polling wait (no sleep hint) for the waits on the per-step critical path: the MMA
+// issuer's, and the softmax's wait for its scores and for its previous P.V. With mbar_wait's
+// sleep hint each of them took a few hundred cycles to resume after the phase completed.
+__device__ __forceinline__ bool mma_wait(uint64_t* bar, uint32_t parity, volatile uint32_t* abort_flag, int code) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const unsigned long long t0 = global_ns();
+    for (;;) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (*abort_flag) return false;
+        if (global_ns() - t0 > kWaitLimitNs) {
+            *abort_flag = 1u;
+            atomicExch(&g_dev_error, code);
+            return false;
+        }
+    }
+}
+
 __host__ __device__ constexpr uint32_t idesc_bf16(int m, int n, bool b_mn_major) {
     return (1u << 4) | (1u << 7) | (1u << 10) | ((b_mn_major ? 1u : 0u) << 16) |
            (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
@@ -109,18 +126,8 @@ __device__ __forceinline__ unsigned long long f2_fma(unsigned long long a, unsig
     return r;
 }
 
-// 2^x0 and 2^x1 with one MUFU operation: the exponents rounded to an f16 pair (for the
-// x <= 8 that occur here, within 2^-12 relative: p moves by at most ~0.3 % where it matters,
-// x >= -16, below the bf16 rounding P gets for the second MMA), ex2.approx.f16x2, widened back.
-// Exponents below the f16 range (x < -24) give 0, as their p are below 2^-24.
-__device__ __forceinline__ void exp2_pair(float x0, float x1, float& p0, float& p1) {
-    uint32_t h, e;
-    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(x1), "f"(x0));
-    asm("ex2.approx.f16x2 %0, %1;" : "=r"(e) : "r"(h));
-    asm("{\n\t.reg .f16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\tcvt.f32.f16 %0, lo;\n\tcvt.f32.f16 %1, hi;\n\t}"
-        : "=f"(p0), "=f"(p1) : "r"(e));
-}
-
+// 2^x on the MUFU unit. Measured on B200: ex2.approx.f16x2 runs at half the rate of the f32 form
+// (the same exponentials per cycle) and its f16 pack costs as much again, so the f32 form is used.
 __device__ __forceinline__ float fast_exp2(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -252,7 +259,7 @@ attention_fwd_kernel(const __grid_constant__ CUtensorMap tmap_qkv, const AttnArg
             constexpr uint32_t idesc_qk = idesc_bf16(ATT_BM, ATT_BN, false);
             constexpr uint32_t idesc_pv = idesc_bf16(ATT_BM, ATT_D, true);
             const int nkv[2] = {nkv_a, nkv_b};
-            bool ok = mbar_wait(q_full, 0, abort_flag, MICA_DEV_TIMEOUT_MMA);
+            bool ok = mma_wait(q_full, 0, abort_flag, MICA_DEV_TIMEOUT_MMA);
             // S = Q_X K_j^T; the fills of S alternate between the tiles and each waits until the
             // previous one has been read (s_free completes once per fill)
             int fills = 0;
@@ -262,7 +269,7 @@ attention_fwd_kernel(const __grid_constant__ CUtensorMap tmap_qkv, const AttnArg
             const uint64_t v_desc0 = smem_desc_sw128(smem_u32(sv), ATT_HALF_BYTES, 1024);
             constexpr uint64_t kTileStep = ATT_TILE_BYTES >> 4;
             auto scores = [&](int x, int j) {
-                if (fills > 0 && !mbar_wait(s_free, (fills - 1) & 1u, abort_flag, MICA_DEV_TIMEOUT_MMA)) return false;
+                if (fills > 0 && !mma_wait(s_free, (fills - 1) & 1u, abort_flag, MICA_DEV_TIMEOUT_MMA)) return false;
                 tc_fence_after();
                 const uint64_t qd = q_desc0 + static_cast<uint64_t>(x) * kTileStep;
                 const uint64_t kd = k_desc0 + static_cast<uint64_t>(j % ATT_K_STAGES) * kTileStep;
@@ -277,7 +284,7 @@ attention_fwd_kernel(const __grid_constant__ CUtensorMap tmap_qkv, const AttnArg
             };
             // O_X += P_X V_j once tile X's softmax has written P_X(j)
             auto values = [&](int x, int j) {
-                if (!mbar_wait(&p_full[x], j & 1u, abort_flag, MICA_DEV_TIMEOUT_MMA)) return false;
+                if (!mma_wait(&p_full[x], j & 1u, abort_flag, MICA_DEV_TIMEOUT_MMA)) return false;
                 tc_fence_after();
                 const uint64_t vd = v_desc0 + static_cast<uint64_t>(j % ATT_V_STAGES) * kTileStep;
                 const uint32_t d_o = tmem + 256 + x * 128, a_p = tmem + 128 + x * 64;
@@ -289,7 +296,7 @@ attention_fwd_kernel(const __grid_constant__ CUtensorMap tmap_qkv, const AttnArg
                 return true;
             };
             auto k_ready = [&](int j) {
-                return mbar_wait(&k_full[j % ATT_K_STAGES], (j / ATT_K_STAGES) & 1u, abort_flag, MICA_DEV_TIMEOUT_MMA);
+                return mma_wait(&k_full[j % ATT_K_STAGES], (j / ATT_K_STAGES) & 1u, abort_flag, MICA_DEV_TIMEOUT_MMA);
             };
             ok = ok && k_ready(0) && (nkv[0] == 0 || scores(0, 0)) && scores(1, 0);
             if (ok) mma_commit(&k_empty[0]);
@@ -297,7 +304,7 @@ attention_fwd_kernel(const __grid_constant__ CUtensorMap tmap_qkv, const AttnArg
                 const bool next = j + 1 < nkv_b;
                 if (next && !k_ready(j + 1)) { ok = false; break; }
                 if (j + 1 < nkv[0] && !scores(0, j + 1)) { ok = false; break; }
-                if (!mbar_wait(&v_full[j % ATT_V_STAGES], (j / ATT_V_STAGES) & 1u, abort_flag, MICA_DEV_TIMEOUT_MMA)) {
+                if (!mma_wait(&v_full[j % ATT_V_STAGES], (j / ATT_V_STAGES) & 1u, abort_flag, MICA_DEV_TIMEOUT_MMA)) {
                     ok = false;
                     break;
                 }
@@ -330,7 +337,7 @@ attention_fwd_kernel(const __grid_constant__ CUtensorMap tmap_qkv, const AttnArg
         bool ok = true;
         for (int j = 0; j < nkv; ++j) {
             bool w = true;
-            if (lane == 0) w = mbar_wait(&s_full[x], j & 1u, abort_flag, MICA_DEV_TIMEOUT_EPILOGUE);
+            if (lane == 0) w = mma_wait(&s_full[x], j & 1u, abort_flag, MICA_DEV_TIMEOUT_EPILOGUE);
             if (!__shfl_sync(0xffffffffu, w, 0)) { ok = false; break; }
             tc_fence_after();
             uint32_t sr[128];
@@ -369,8 +376,8 @@ attention_fwd_kernel(const __grid_constant__ CUtensorMap tmap_qkv, const AttnArg
                 alpha = fast_exp2(m_use - mx);
                 m_use = mx;
             }
-            // p = 2^(s c - m): one f32x2 fma per two scores, one paired exp2, one f32x2 add into
-            // four partial sums, one bf16x2 pack
+            // p = 2^(s c - m): one f32x2 fma per two scores, two exp2, one f32x2 add into four
+            // partial sums, one bf16x2 pack
             const unsigned long long c2 = f2_pack(c, c);
             const unsigned long long nm2 = f2_pack(-m_use, -m_use);
             unsigned long long sp[4] = {0ull, 0ull, 0ull, 0ull};
@@ -381,8 +388,7 @@ attention_fwd_kernel(const __grid_constant__ CUtensorMap tmap_qkv, const AttnArg
                                                      c2, nm2);
                 float x0, x1;
                 f2_unpack(x2, x0, x1);
-                float p0, p1;
-                exp2_pair(x0, x1, p0, p1);
+                const float p0 = fast_exp2(x0), p1 = fast_exp2(x1);
                 sp[i & 3] = f2_add(sp[i & 3], f2_pack(p0, p1));
                 pk[i] = pack_bf16(p0, p1);
             }
@@ -394,7 +400,7 @@ attention_fwd_kernel(const __grid_constant__ CUtensorMap tmap_qkv, const AttnArg
             l = l * alpha + (((a0 + a1) + (b0 + b1)) + ((d0 + d1) + (e0 + e1)));
             // P_X and O_X are free again once the previous P.V is done
             if (j >= 1) {
-                if (lane == 0) w = mbar_wait(&pv_done[x], (j - 1) & 1u, abort_flag, MICA_DEV_TIMEOUT_EPILOGUE);
+                if (lane == 0) w = mma_wait(&pv_done[x], (j - 1) & 1u, abort_flag, MICA_DEV_TIMEOUT_EPILOGUE);
                 if (!__shfl_sync(0xffffffffu, w, 0)) { ok = false; break; }
                 tc_fence_after();
             }
