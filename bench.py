@@ -567,7 +567,22 @@ def run_prefill(dev, rank, world, batch_tokens=16384):
     b.synchronize()
     ms = a.elapsed_time(b) / reps
     out['config3_32k'] = {'ms_per_request': round(ms, 2), 'tokens_per_s_per_gpu': round(32768 / ms * 1e3),
-                          'prob_sum': round(float(p.sum()), 6)}
+                          'prob_sum': round(float(p.sum()), 6), 'attention': 'torch SDPA (cuDNN)'}
+    # the same request with this library's tcgen05 attention in the 35 full-length layers
+    pf_m = P.Prefill(model, options, max_len=32768, attention='mica')
+    for _ in range(2):
+        pf_m.score(ids, 2, 257, graphs=False)
+    torch.cuda.synchronize(dev)
+    a.record()
+    for _ in range(reps):
+        z_m, p_m = pf_m.score(ids, 2, 257, graphs=False)
+    b.record()
+    b.synchronize()
+    ms_m = a.elapsed_time(b) / reps
+    out['config3_32k_mica_attention'] = {'ms_per_request': round(ms_m, 2),
+                                         'tokens_per_s_per_gpu': round(32768 / ms_m * 1e3),
+                                         'max_abs_dp_vs_sdpa': float((p_m - p).abs().max())}
+    del pf_m
     # config 4: 256 requests sharded over the ranks; each rank scores its share in batches of
     # similar length (sorted, padded to 64-token buckets, up to batch_tokens rows per pass)
     from mica_b200.shard import lpt_shard, per_rank, plan_batches

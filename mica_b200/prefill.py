@@ -365,7 +365,16 @@ class _Normed:
 class Prefill:
     """Scores requests on a Decoder: ids -> option probabilities of the last position."""
 
-    def __init__(self, model: Decoder, option_ids, max_len: int = 32768, attn_backends=None):
+    def __init__(self, model: Decoder, option_ids, max_len: int = 32768, attn_backends=None, attention: str = 'sdpa'):
+        """attention: 'sdpa' runs the causal attention of the full-length layers through torch SDPA
+        (cuDNN first, `attn_backends`); 'mica' runs it with this library's tcgen05 kernel
+        (mica_attention_prefill), reading q/k/v in place from the QKV projection's output. The
+        last layer's last-row attention uses SDPA either way."""
+        if attention not in ('sdpa', 'mica'):
+            raise ValueError(f"attention must be 'sdpa' or 'mica', not {attention!r}")
+        if attention == 'mica' and model.cfg.head_dim != 128:
+            raise ValueError(f"attention='mica' needs head_dim 128, not {model.cfg.head_dim}")
+        self.attention = attention
         self.m = model
         cfg = model.cfg
         dev = model.device
@@ -473,9 +482,14 @@ class Prefill:
             qkv = self._qkv_cols(lay, nq, 0, lay.qkv_w.shape[0])
             torch.ops.mica.qk_norm_rope(qkv, lay.q_norm, lay.k_norm, self.cos, self.sin, pos, 0, cfg.heads,
                                         cfg.kv_heads, cfg.eps)
-            q, k, v = qkv.split([cfg.q_dim, cfg.kv_dim, cfg.kv_dim], dim=1)
-            attn = self._attention(q.view(B, L, cfg.heads, cfg.head_dim), k.view(B, L, cfg.kv_heads, cfg.head_dim),
-                                   v.view(B, L, cfg.kv_heads, cfg.head_dim), causal=True)
+            if self.attention == 'mica':
+                # each request attends causally within its own L rows; padding rows sit after a
+                # request's real rows, so no real row sees them
+                attn = torch.ops.mica.attention_prefill(qkv, B, L, cfg.heads, cfg.kv_heads, self.scale)
+            else:
+                q, k, v = qkv.split([cfg.q_dim, cfg.kv_dim, cfg.kv_dim], dim=1)
+                attn = self._attention(q.view(B, L, cfg.heads, cfg.head_dim), k.view(B, L, cfg.kv_heads, cfg.head_dim),
+                                       v.view(B, L, cfg.kv_heads, cfg.head_dim), causal=True)
             qa, sa = torch.ops.mica.act_quant(attn, lay.o_inv, K._round_code())
             o = self._gemm(qa, sa, lay.o_w, lay.o_s, lay.o_b)
             nm, h = self._normed(o, lay.post_norm, h, lay.mlp_in_inv(), lay.distinct_mlp_invs())

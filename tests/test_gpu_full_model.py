@@ -61,15 +61,18 @@ def full():
     torch.cuda.empty_cache()
 
 
+@pytest.mark.parametrize('attention', ['sdpa', 'mica'])
 @pytest.mark.parametrize('n', FM.LENGTHS)
-def test_full_scale_option_probs_within_the_reference_self_spread(full, n):
+def test_full_scale_option_probs_within_the_reference_self_spread(full, n, attention):
+    """attention 'mica' runs the 35 full-length layers' attention on this library's tcgen05
+    kernel instead of cuDNN: the same bar holds."""
     import mica_b200.int8_kernels as K
     from mica_b200 import prefill as P
     model, g, band = full
     ids, rows = FM.request(n)
     assert np.array_equal(ids.numpy(), g[f'n{n}/ids']) and np.array_equal(rows.numpy(), g[f'n{n}/rows'])
     lo, hi = (int(v) for v in g[f'n{n}/slice'])
-    pf = P.Prefill(model, rows, max_len=max(FM.LENGTHS))
+    pf = P.Prefill(model, rows, max_len=max(FM.LENGTHS), attention=attention)
     K.ROUND['mode'] = 'half_even'      # the reference's QLinear 'emulate' path rounds half to even
     try:
         z, p = pf.score(ids.cuda(), lo, hi, graphs=False)
@@ -80,7 +83,7 @@ def test_full_scale_option_probs_within_the_reference_self_spread(full, n):
     self_p = np.abs(ref_p - band[f'n{n}/probs']).max()        # the reference against itself
     self_z = np.abs(ref_z - band[f'n{n}/logits']).max()
     dp, dz = np.abs(p - ref_p).max(), np.abs(z - ref_z).max()
-    print(f'{n} tokens: max |dp| {dp:.3g} (reference self-spread {self_p:.3g}, probs up to {ref_p.max():.3g}); '
+    print(f'{n} tokens, {attention}: max |dp| {dp:.3g} (reference self-spread {self_p:.3g}, probs up to {ref_p.max():.3g}); '
           f'max |dz| {dz:.3g} (self-spread {self_z:.3g})')
     assert dp <= 2 * self_p
     assert dz <= 2 * self_z

@@ -175,13 +175,14 @@ def test_startup_selftest_like_the_reference():
     assert res['worst_ratio'] <= rt.SELFTEST_TOL
 
 
-def test_batched_scoring_matches_single_requests():
+@pytest.mark.parametrize('attention', ['sdpa', 'mica'])
+def test_batched_scoring_matches_single_requests(attention):
     """[B, L] batches (padded, per-request limits and option slices) give each request the
-    probabilities it gets alone (within attention-kernel rounding)."""
+    probabilities it gets alone (within attention-kernel rounding), with either attention."""
     from mica_b200 import prefill as P
     cfg = P.DecoderConfig(layers=3, vocab=4096)
     model = P.random_decoder(cfg, torch.device('cuda'), seed=21)
-    pf = P.Prefill(model, torch.arange(0, 257), max_len=4096)
+    pf = P.Prefill(model, torch.arange(0, 257), max_len=4096, attention=attention)
     gen = torch.Generator().manual_seed(8)
     lens = [300, 511, 64, 1000, 777]
     ids = [torch.randint(0, cfg.vocab, (n,), generator=gen).cuda() for n in lens]
@@ -193,14 +194,15 @@ def test_batched_scoring_matches_single_requests():
         assert abs(float(pb[i].sum()) - 1.0) < 1e-4
 
 
-def test_batch_graph_replay_matches_eager_batch():
+@pytest.mark.parametrize('attention', ['sdpa', 'mica'])
+def test_batch_graph_replay_matches_eager_batch(attention):
     """A captured [B, L] batch graph replays each new batch (ids, limits and option slices
     copied into its static buffers) with the eager batch's results, and its outputs are the
     caller's own (a later replay does not overwrite them)."""
     from mica_b200 import prefill as P
     cfg = P.DecoderConfig(layers=3, vocab=4096)
     model = P.random_decoder(cfg, torch.device('cuda'), seed=22)
-    pf = P.Prefill(model, torch.arange(0, 257), max_len=4096)
+    pf = P.Prefill(model, torch.arange(0, 257), max_len=4096, attention=attention)
     gen = torch.Generator().manual_seed(12)
     batches = [[300, 511, 64, 1000], [1024, 700, 1, 999]]
     ids = [[torch.randint(0, cfg.vocab, (n,), generator=gen).cuda() for n in lens] for lens in batches]
@@ -256,3 +258,32 @@ def test_int8_file_model_probs_match_reference(int8_file_model, i):
     assert np.abs(z.cpu().numpy() - ref_z).max() < 2e-2 * max(1.0, float(np.abs(ref_z).max()))
     assert torch.allclose(pg, p, atol=1e-3, rtol=0)                     # graph replay vs eager
     assert np.abs(p_full.cpu().numpy() - p.cpu().numpy()).max() < 1e-3   # last-row restriction
+
+
+def test_mica_attention_matches_sdpa_in_the_prefill():
+    """The same 3-layer 4B-width decoder scored with this library's attention and with SDPA
+    (cuDNN). Per-token int8 requantisation turns attention rounding into quantisation-noise-sized
+    differences, so the bar is the spread between two of torch's own attention kernels (cuDNN
+    against flash, or the math kernel where flash is absent) on the same model: within 3x that,
+    plus 1e-3."""
+    from torch.nn.attention import SDPBackend
+    from mica_b200 import prefill as P
+    cfg = P.DecoderConfig(layers=3, vocab=4096)
+    model = P.random_decoder(cfg, torch.device('cuda'), seed=23)
+    cudnn = P.Prefill(model, torch.arange(0, 257), max_len=4096, attn_backends=[SDPBackend.CUDNN_ATTENTION])
+    eff = P.Prefill(model, torch.arange(0, 257), max_len=4096,
+                    attn_backends=[SDPBackend.FLASH_ATTENTION, SDPBackend.MATH])
+    mica = P.Prefill(model, torch.arange(0, 257), max_len=4096, attention='mica')
+    gen = torch.Generator().manual_seed(13)
+    for n in (2048, 4000):
+        ids = torch.randint(0, cfg.vocab, (n,), generator=gen).cuda()
+        _, pc = cudnn.score(ids, 2, 257, graphs=False)
+        _, pe = eff.score(ids, 2, 257, graphs=False)
+        _, pm = mica.score(ids, 2, 257, graphs=False)
+        spread = float((pe - pc).abs().max())
+        dp = float((pm - pc).abs().max())
+        print(f'{n} tokens: mica vs cuDNN {dp:.3g}, flash vs cuDNN {spread:.3g}')
+        assert dp <= 3 * spread + 1e-3, (dp, spread)
+        assert abs(float(pm.sum()) - 1.0) < 1e-5
+    with pytest.raises(ValueError):
+        P.Prefill(model, torch.arange(0, 257), max_len=4096, attention='flash')
