@@ -72,7 +72,29 @@ struct GemmArgs {
     long ldq;
     float* s_out;         // [M]
     const float* inv_h;   // [I] or nullptr: down_proj's inv_smooth, applied before the requant
+    int panel;            // n-tiles per weight panel (tile_origin); 0 = row-major over all of N
 };
+
+// Origin (m-tile, n-tile) of persistent tile `tile` in an num_m x num_n grid. With panel > 0 the
+// n-tiles are cut into panels of `panel` columns and each panel is swept over all of M (m-major
+// inside the panel), so consecutive waves share one panel of weights and it stays in L2; row-major
+// order makes every wave touch all N x K weight bytes. Odd panels sweep M backwards, so a panel
+// starts on the activation rows the previous one read last, which L2 still holds. The last panel
+// may be narrower.
+__device__ __forceinline__ void tile_origin(int tile, int num_m, int num_n, int panel, int& mt, int& nt) {
+    if (panel <= 0 || panel >= num_n) {
+        mt = tile / num_n;
+        nt = tile % num_n;
+        return;
+    }
+    const int per = num_m * panel;               // tiles in a full panel
+    const int p = tile / per;
+    const int n_base = p * panel;
+    const int w = min(panel, num_n - n_base);
+    const int u = tile - p * per;
+    mt = (p & 1) ? num_m - 1 - u / w : u / w;
+    nt = n_base + u % w;
+}
 
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
     __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
@@ -331,8 +353,10 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
             bool ok = true;
             const uint64_t pol_b = policy_evict_last();   // weights: re-read by every M block
             for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-                const int m0 = (tile / num_n) * S::BM;
-                const int n0 = (tile % num_n) * BN;
+                int mt, nt;
+                tile_origin(tile, num_m, num_n, args.panel, mt, nt);
+                const int m0 = mt * S::BM;
+                const int n0 = nt * BN;
                 for (int kb = 0; kb < num_kb; ++kb, ++it) {
                     const int st = it % STAGES;
                     const uint32_t ph = (it / STAGES) & 1u;
@@ -413,8 +437,10 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
         // The dequantised output is written once: evict it before the weights (evict_last).
         const uint64_t pol_c = policy_evict_first();
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
-            const int m0 = (tile / num_n) * S::BM;
-            const int n0 = (tile % num_n) * BN;
+            int mt, nt;
+            tile_origin(tile, num_m, num_n, args.panel, mt, nt);
+            const int m0 = mt * S::BM;
+            const int n0 = nt * BN;
             const int acc = local & 1;
             const uint32_t acc_ph = (local >> 1) & 1;
             bool w = true;

@@ -117,8 +117,10 @@ gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
             const uint64_t pol_b = policy_evict_last();
             const uint64_t pol_a = policy_evict_normal();  // activations: re-read by every N tile
             for (int tile = cluster_id; tile < num_tiles && ok; tile += num_clusters) {
-                const int m0 = (tile / num_n) * S::BM;
-                const int n0 = (tile % num_n) * BN;
+                int mt, nt;
+                tile_origin(tile, num_m, num_n, args.panel, mt, nt);
+                const int m0 = mt * S::BM;
+                const int n0 = nt * BN;
                 for (int kb = 0; kb < num_kb; ++kb, ++it) {
                     const int st = it % STAGES;
                     const uint32_t ph = (it / STAGES) & 1u;
@@ -198,8 +200,10 @@ gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
         constexpr int CHUNKS_PER_BOX = COLS_PER_BOX / 32;
         constexpr int BOXES = BN / COLS_PER_BOX;
         for (int tile = cluster_id; tile < num_tiles; tile += num_clusters, ++local) {
-            const int m0 = (tile / num_n) * S::BM;
-            const int n0 = (tile % num_n) * BN;
+            int mt, nt;
+            tile_origin(tile, num_m, num_n, args.panel, mt, nt);
+            const int m0 = mt * S::BM;
+            const int n0 = nt * BN;
             const int acc = local & 1;
             const uint32_t acc_ph = (local >> 1) & 1;
             bool w = true;

@@ -401,6 +401,20 @@ struct GemmPlan {
     size_t ws_bytes;
 };
 
+// Weight panel for multi-wave persistent grids (tile_origin): weights of more than kPanelBytes
+// (N x K int8) are swept in near-equal panels of at most that size, each over all of M. Measured
+// on the 49.8 MB gate_up weights at M = 32768, row-major order read them about eight times from
+// DRAM; one 25 MB panel stays in L2 across the waves that use it, at the price of reading A once
+// per panel.
+constexpr size_t kPanelBytes = static_cast<size_t>(24) << 20;
+static int gemm_panel(int N, int K, int bn) {
+    const size_t wb = static_cast<size_t>(N) * static_cast<size_t>(K);
+    if (wb <= kPanelBytes) return 0;
+    const int num_n = (N + bn - 1) / bn;
+    const int panels = static_cast<int>((wb + kPanelBytes - 1) / kPanelBytes);
+    return (num_n + panels - 1) / panels;
+}
+
 static int gemm_tile_args_ok(int block_m, int block_n, int max_ctas, int splits) {
     if (block_m != 0 && block_m != 128 && block_m != 256) return MICA_ERR_ARG;
     if (block_n != 0 && block_n != 64 && block_n != 128 && block_n != 256 && block_n != 320) return MICA_ERR_ARG;
@@ -733,6 +747,7 @@ int mica_w8a8_gemm_ex(const int8_t* A, long lda, const int8_t* B, long ldb, cons
         return rc;
     GemmArgs g = {};
     g.sa = sa; g.sb = sb; g.bias = bias; g.M = M; g.N = N; g.K = K;
+    g.panel = gemm_panel(N, K, bn);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (bm == 256) {
         const long tiles = static_cast<long>((M + 255) / 256) * ((N + bn - 1) / bn);
@@ -840,6 +855,7 @@ int mica_w8a8_gemm_swiglu_quant(const int8_t* A, long lda, const int8_t* Bgu, lo
     g.row_amax = amax; g.grid_sync = sync;
     g.h = static_cast<const __nv_bfloat16*>(h_out); g.ldh = ldh; g.q_out = q_out; g.ldq = ldq; g.s_out = s_out;
     g.inv_h = inv_h;
+    g.panel = gemm_panel(N, K, bn);
     const long tiles = static_cast<long>((M + 127) / 128) * ((N + bn - 1) / bn);
     const int grid = static_cast<int>(tiles < sms ? tiles : sms);
     if (bn == 256) return gemm_launch<256, EPI_SWIGLU, __nv_bfloat16, 8>(ta, tb, th, g, grid, true, st);
