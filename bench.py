@@ -389,7 +389,7 @@ def run_mica(args, rank, world, local):
         'gpu_launches': launches_per_step * args.steps,
         'roofline': {'bound': 'tensor', 'achieved': round(achieved, 1), 'peak': round(peak_int8, 1),
                      'unit': 'TOPS (int8)', 'frac': round(achieved / peak_int8, 4), 'traffic': traffic,
-                     'traffic_note': ('DRAM bytes per GEMM launch, mean over the sweep, one ncu capture '
+                     'traffic_note': ('DRAM bytes per GEMM launch, mean over the sweep, one ncu capture per shape '
                                       '(profiles/gemm_i8_traffic.json); algorithmic bytes per launch '
                                       f'(A + B + bf16 C + scales) {alg_bytes}'),
                      'peak_source': f"2 x {pk['source']} bf16 dense ({pk['bf16']} TFLOP/s); nominal dense int8 4500",
