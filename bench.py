@@ -669,8 +669,9 @@ def run_reference(args):
 
 def run_shape(args):
     """One kernel on one shape, for profiler captures (--kernel gemm | swiglu | act_quant |
-    rmsnorm_quant | readout): `--warmup` untimed launches, then `--steps` launches.
-    Prints the mean device time per launch (back-to-back launches, CUDA events)."""
+    rmsnorm_quant | readout | attention): `--warmup` untimed launches, then `--steps` launches.
+    Prints the mean time per launch of those back-to-back launches (CUDA events), and graph_us:
+    the device time of one call replayed in a graph with an L2 flush before each."""
     import torch
     import mica_b200.int8_kernels as K
     from mica_b200 import _native as Nat
@@ -749,8 +750,12 @@ def run_shape(args):
     ms = a.elapsed_time(b) / args.steps
     unit, amount = work
     rate = amount / ms / 1e9 if unit in ('TOPS', 'TFLOP/s') else amount / ms / 1e6
+    # the same call device-timed inside a graph, L2 flushed before each (after the launches above,
+    # so a profiler's launch count over them is unchanged); small shapes are launch-bound above
+    us_g = graph_time(dev, fn, max(3, min(args.steps, 20)))
+    rate_g = amount / us_g / 1e6 if unit in ('TOPS', 'TFLOP/s') else amount / us_g / 1e3
     print(json.dumps({'kernel': args.kernel, 'shape': [m, n, k], 'tile': args.tile, 'ms_per_launch': round(ms, 4),
-                      unit: round(rate, 1)}), flush=True)
+                      unit: round(rate, 1), 'graph_us': round(us_g, 2), f'graph_{unit}': round(rate_g, 1)}), flush=True)
 
 
 def run_sweep_launches(args, dev):

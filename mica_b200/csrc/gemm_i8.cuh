@@ -36,11 +36,12 @@ struct GemmShape {
     static constexpr int BOX_BYTES = 32 * 128;          // one 32-row x 128-byte store box
     static constexpr int BOX_BUFS = EW == 4 ? 2 : 1;    // store boxes per epilogue warp
     static constexpr int EPI_BYTES = EPI_WARPS * BOX_BUFS * BOX_BYTES;
+    static constexpr int COL_BYTES = BN * 4;            // the current tile's column scales (dequant)
     static constexpr int AUX_BYTES = 256;               // mbarriers, TMEM address, abort flag
     static constexpr int SMEM_OPTIN = 232448;           // sm_100 opt-in shared memory per block
-    static constexpr int STAGES_RAW = (SMEM_OPTIN - 1024 - EPI_BYTES - AUX_BYTES) / STAGE_BYTES;
+    static constexpr int STAGES_RAW = (SMEM_OPTIN - 1024 - EPI_BYTES - COL_BYTES - AUX_BYTES) / STAGE_BYTES;
     static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
-    static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + AUX_BYTES;
+    static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + COL_BYTES + AUX_BYTES;
     static constexpr int ACC_COLS = BN;                 // int32 accumulator columns per buffer
     // BN = 320 (wider than one MMA or one TMA box): two 160-wide halves per k-step, and one
     // accumulator buffer only (2 x 320 columns exceed the 512 of tensor memory), so the host
@@ -212,17 +213,26 @@ __device__ __forceinline__ void dequant_chunk_packed(const uint32_t (&r)[32], fl
     }
 }
 
+// The column scales of one 32-column chunk as eight uniform 16-byte loads, when the chunk is
+// vectorisable (else nothing: its gathered form loads its own). The CTA-pair kernel issues them
+// one chunk ahead of use (gemm_i8_kernel stages a whole tile's in shared memory instead): a chunk
+// that loads its scales at its own start waits an L2 round trip.
+__device__ __forceinline__ void load_sb4(const GemmArgs& a, int gcol0, int N, float4 (&sb4)[8]) {
+    if (chunk_vectorisable(a, gcol0, N)) {
+#pragma unroll
+        for (int v = 0; v < 8; ++v) sb4[v] = __ldg(reinterpret_cast<const float4*>(a.sb + gcol0) + v);
+    }
+}
+
 // One 32-column chunk of the dequant epilogue: tensor-memory load of the lane's row, then the
-// packed form when the chunk's column vectors allow it, else the gathered form.
+// packed form (with the chunk's scales sb4 already loaded by load_sb4) when the chunk's column
+// vectors allow it, else the gathered form.
 template <typename OutT>
 __device__ __forceinline__ void dequant_chunk(const GemmArgs& args, uint32_t t_addr, int gcol0, int N, float sa_v,
-                                              uint32_t box_row, int cc) {
+                                              const float4 (&sb4)[8], uint32_t box_row, int cc) {
     const int lane = threadIdx.x & 31;
     uint32_t r[32];
     if (chunk_vectorisable(args, gcol0, N)) {
-        float4 sb4[8];
-#pragma unroll
-        for (int v = 0; v < 8; ++v) sb4[v] = __ldg(reinterpret_cast<const float4*>(args.sb + gcol0) + v);
         tmem_ld_32x32b_x32(t_addr, r);
         tmem_ld_wait();
         dequant_chunk_packed<OutT>(r, sa_v, sb4, args.bias != nullptr ? args.bias + gcol0 : nullptr, box_row, cc);
@@ -234,6 +244,23 @@ __device__ __forceinline__ void dequant_chunk(const GemmArgs& args, uint32_t t_a
         tmem_ld_wait();
         dequant_chunk_to_box<OutT>(r, sa_v, sb_l, bias_l, args.bias != nullptr, box_row, cc);
     }
+}
+
+// The SwiGLU epilogue's per-lane column values of one 32-column chunk at tile column col0: lane
+// j's gate/up scale and bias of column col0 + j, and down_proj's smoothing of h column
+// col0 / 2 + (j & 15). Loaded one chunk ahead of use, as load_sb4.
+struct SwigluCols {
+    float sb, bias, inv;
+};
+__device__ __forceinline__ SwigluCols load_swiglu_cols(const GemmArgs& a, int gcol0, int N) {
+    const int lane = threadIdx.x & 31;
+    const int gcol = gcol0 + lane;
+    const int hcol = gcol0 / 2 + (lane & 15);
+    SwigluCols c;
+    c.sb = gcol < N ? a.sb[gcol] : 0.f;
+    c.bias = (a.bias != nullptr && gcol < N) ? a.bias[gcol] : 0.f;
+    c.inv = (a.inv_h != nullptr && hcol < N / 2) ? a.inv_h[hcol] : 1.f;
+    return c;
 }
 
 // f[e] = RN(f[e] * inv[e]) for eight consecutive columns (inv 16-byte aligned).
@@ -302,13 +329,16 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
     uint8_t* smem_a = smem;                                   // STAGES x A_BYTES
     uint8_t* smem_b = smem + STAGES * S::A_BYTES;             // STAGES x B_BYTES
     uint8_t* smem_epi = smem_b + STAGES * S::B_BYTES;         // 4 warps x 2 boxes
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem_epi + S::EPI_BYTES);
+    float* smem_cols = reinterpret_cast<float*>(smem_epi + S::EPI_BYTES);   // BN column scales
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem_epi + S::EPI_BYTES + S::COL_BYTES);
     uint64_t* full_bar = bars;                                // [STAGES]  TMA -> MMA
     uint64_t* empty_bar = bars + STAGES;                      // [STAGES]  MMA -> TMA
     uint64_t* tfull_bar = bars + 2 * STAGES;                  // [2]       MMA -> epilogue
     uint64_t* tempty_bar = bars + 2 * STAGES + 2;             // [2]       epilogue -> MMA
     uint64_t* drain_bar = bars + 2 * STAGES + 4;              // [1]       teardown
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
+    uint64_t* cols_full = bars + 2 * STAGES + 5;              // [1]       epilogue: tile's scales stored
+    uint64_t* cols_free = bars + 2 * STAGES + 6;              // [1]       epilogue: tile's scales read
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 7);
     volatile uint32_t* abort_flag = tmem_slot + 1;
 
     const int M = args.M, N = args.N, K = args.K;
@@ -334,6 +364,8 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
             mbar_init(&tempty_bar[i], S::EPI_WARPS * 32);
         }
         mbar_init(drain_bar, 1);
+        mbar_init(cols_full, EW);
+        mbar_init(cols_free, EW);
         *abort_flag = 0u;
         fence_mbar_init();
         tma_prefetch_desc(&tmap_a);
@@ -443,13 +475,48 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
             const int n0 = nt * BN;
             const int acc = local & 1;
             const uint32_t acc_ph = (local >> 1) & 1;
+            // The tile's row scale and column vectors do not depend on the accumulator: start their
+            // loads before waiting for it, so a cold L2 (first tile, small grids) costs no DRAM round
+            // trips after the main loop. One 32-column line per lane.
+            const int grow = m0 + row_local;
+            const float sa_v = grow < M ? __ldg(args.sa + grow) : 0.f;
+            if (lane * 32 < BN && n0 + lane * 32 < N) {
+                prefetch_l1(args.sb + n0 + lane * 32);
+                if (args.bias != nullptr) prefetch_l1(args.bias + n0 + lane * 32);
+            }
+            if constexpr (EPI == EPI_SWIGLU) {
+                if (args.inv_h != nullptr && lane * 32 < BN / 2 && (n0 / 2) + lane * 32 < N / 2)
+                    prefetch_l1(args.inv_h + n0 / 2 + lane * 32);
+            }
+            // Dequant: the tile's BN column scales go to shared memory while the accumulator is
+            // computed (cols_free: every epilogue warp is done with the previous tile's; cols_full:
+            // all of this tile's are stored; one arrival per warp, bounded waits). Measured on B200, a chunk that loaded its scales at
+            // its own start waited ~450 cycles for L2, which on one-tile-per-CTA grids left ~1.4 us
+            // of epilogue exposed per warp; the values do not stay in the small L1 beside 227 KB of
+            // shared memory. SwiGLU: the first chunk's per-lane values, loaded one chunk ahead.
+            SwigluCols sw_cur;
+            if constexpr (EPI == EPI_DEQUANT) {
+                bool cw = true;
+                if (lane == 0 && local > 0)
+                    cw = mbar_wait(cols_free, (local - 1) & 1, abort_flag, MICA_DEV_TIMEOUT_EPILOGUE);
+                if (!__shfl_sync(0xffffffffu, cw, 0)) break;
+                for (int c = ew * 32 + lane; c < BN; c += EW * 32)
+                    smem_cols[c] = n0 + c < N ? __ldg(args.sb + n0 + c) : 0.f;
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(cols_full);
+                    cw = mbar_wait(cols_full, local & 1, abort_flag, MICA_DEV_TIMEOUT_EPILOGUE);
+                }
+                if (!__shfl_sync(0xffffffffu, cw, 0)) break;
+                __syncwarp();                  // orders the lanes' reads after lane 0's acquire
+            } else {
+                sw_cur = load_swiglu_cols(args, n0 + part * 128, N);
+            }
             bool w = true;
             if (lane == 0) w = mbar_wait(&tfull_bar[acc], acc_ph, abort_flag, MICA_DEV_TIMEOUT_EPILOGUE);
             if (!__shfl_sync(0xffffffffu, w, 0)) break;
             tc_fence_after();
 
-            const int grow = m0 + row_local;
-            const float sa_v = grow < M ? args.sa[grow] : 0.f;
             const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q4 * 32) << 16) + acc * S::ACC_COLS;
 
             if constexpr (EPI == EPI_DEQUANT) {
@@ -469,12 +536,16 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
 #pragma unroll
                     for (int cc = 0; cc < CHUNKS_PER_BOX; ++cc) {
                         const int col0 = bx * COLS_PER_BOX + cc * 32;
-                        dequant_chunk<OutT>(args, t_row + col0, n0 + col0, N, sa_v, box_row, cc);
+                        float4 sb4[8];             // uniform shared loads: one broadcast each
+#pragma unroll
+                        for (int v = 0; v < 8; ++v) sb4[v] = reinterpret_cast<const float4*>(smem_cols + col0)[v];
+                        dequant_chunk<OutT>(args, t_row + col0, n0 + col0, N, sa_v, sb4, box_row, cc);
                     }
                     if (bx + PARTS >= BOXES) {
                         // this warp's last read of the accumulator: hand it back to the MMA warp
                         tc_fence_before();
                         mbar_arrive(&tempty_bar[acc]);
+                        if (lane == 0) mbar_arrive(cols_free);   // and its last read of the scales
                     }
                     fence_proxy_async_smem();
                     __syncwarp();
@@ -503,12 +574,11 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
 #pragma unroll
                     for (int cc = 0; cc < CHUNKS_PER_BOX; ++cc) {
                         const int col0 = bx * 128 + cc * 32;
-                        const int gcol = n0 + col0 + lane;
-                        const float sb_l = gcol < N ? args.sb[gcol] : 0.f;
-                        const float bias_l = (args.bias != nullptr && gcol < N) ? args.bias[gcol] : 0.f;
-                        // down_proj's smoothing of h column (n0 + col0) / 2 + (lane & 15)
-                        const int hcol = (n0 + col0) / 2 + (lane & 15);
-                        const float inv_l = (args.inv_h != nullptr && hcol < N / 2) ? args.inv_h[hcol] : 1.f;
+                        const float sb_l = sw_cur.sb, bias_l = sw_cur.bias;
+                        const float inv_l = sw_cur.inv;   // down_proj's smoothing of h column (n0 + col0) / 2 + (lane & 15)
+                        // this warp's next chunk's values, in flight while this chunk is processed
+                        const int ncol = cc + 1 < CHUNKS_PER_BOX ? col0 + 32 : (bx + PARTS) * 128;
+                        if (ncol < BN) sw_cur = load_swiglu_cols(args, n0 + ncol, N);
                         uint32_t r[32];
                         tmem_ld_32x32b_x32(t_row + col0, r);
                         tmem_ld_wait();

@@ -206,12 +206,19 @@ gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
             const int n0 = nt * BN;
             const int acc = local & 1;
             const uint32_t acc_ph = (local >> 1) & 1;
+            // row scale and column-vector lines fetched before the accumulator wait (gemm_i8.cuh)
+            const int grow = m0 + row_local;
+            const float sa_v = grow < M ? __ldg(args.sa + grow) : 0.f;
+            if (lane * 32 < BN && n0 + lane * 32 < N) {
+                prefetch_l1(args.sb + n0 + lane * 32);
+                if (args.bias != nullptr) prefetch_l1(args.bias + n0 + lane * 32);
+            }
+            float4 sb_cur[8];                                // the first chunk's scales (load_sb4)
+            load_sb4(args, n0, N, sb_cur);
             bool w = true;
             if (lane == 0) w = mbar_wait(&tfull_bar[acc], acc_ph, abort_flag, MICA_DEV_TIMEOUT_EPILOGUE);
             if (!__shfl_sync(0xffffffffu, w, 0)) break;
             tc_fence_after();
-            const int grow = m0 + row_local;
-            const float sa_v = grow < M ? args.sa[grow] : 0.f;
             const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q4 * 32) << 16) + acc * S::ACC_COLS;
 #pragma unroll 1
             for (int bx = 0; bx < BOXES; ++bx, ++box_count) {
@@ -222,7 +229,14 @@ gemm_i8_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_con
 #pragma unroll
                 for (int cc = 0; cc < CHUNKS_PER_BOX; ++cc) {
                     const int col0 = bx * COLS_PER_BOX + cc * 32;
-                    dequant_chunk<OutT>(args, t_row + col0, n0 + col0, N, sa_v, box_row, cc);
+                    const int ncol = col0 + 32;                  // the next chunk's scales in flight
+                    float4 sb_nxt[8];
+                    if (ncol < BN) load_sb4(args, n0 + ncol, N, sb_nxt);
+                    dequant_chunk<OutT>(args, t_row + col0, n0 + col0, N, sa_v, sb_cur, box_row, cc);
+                    if (ncol < BN) {
+#pragma unroll
+                        for (int v = 0; v < 8; ++v) sb_cur[v] = sb_nxt[v];
+                    }
                 }
                 if (bx == BOXES - 1) {
                     // this warp's last read of the accumulator: one arrival for the warp

@@ -173,6 +173,12 @@ gemm_i8_splitk_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_c
         // this row's int32 partial in the stage buffers: 16-byte chunk c of row r at
         // (c * 128 + r) * 16, so one warp's 32 rows of a chunk are contiguous
         const uint32_t part_row = smem_u32(smem) + static_cast<uint32_t>(row_local) * 16u;
+        // row scale and column-vector lines fetched before the accumulator wait (gemm_i8.cuh)
+        if (m0 + row_local < M) prefetch_l1(args.sa + m0 + row_local);
+        if (lane * 32 < BN && n0 + lane * 32 < N) {
+            prefetch_l1(args.sb + n0 + lane * 32);
+            if (args.bias != nullptr) prefetch_l1(args.bias + n0 + lane * 32);
+        }
         bool w = true;
         if (lane == 0) w = mbar_wait(tfull_bar, 0, abort_flag, MICA_DEV_TIMEOUT_EPILOGUE);
         w = __shfl_sync(0xffffffffu, w, 0);

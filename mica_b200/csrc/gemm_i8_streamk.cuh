@@ -212,6 +212,12 @@ gemm_i8_streamk_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_
             const int acc = local & 1;
             const uint32_t acc_ph = (local >> 1) & 1;
             ++local;
+            // row scale and column-vector lines fetched before any wait (gemm_i8.cuh)
+            if (m0 + row_local < M) prefetch_l1(args.sa + m0 + row_local);
+            if (lane * 32 < BN && n0 + lane * 32 < N) {
+                prefetch_l1(args.sb + n0 + lane * 32);
+                if (args.bias != nullptr) prefetch_l1(args.bias + n0 + lane * 32);
+            }
             const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(q4 * 32) << 16);
             const uint32_t t_row = lane_base + acc * S::ACC_COLS;
             // FINISH (kb0 == 0, kb1 < num_kb): the rest of this tile is CTA cta + 1's STORE. It is
@@ -286,6 +292,10 @@ gemm_i8_streamk_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_
             constexpr int COLS_PER_BOX = 128 / static_cast<int>(sizeof(OutT));
             constexpr int CHUNKS_PER_BOX = COLS_PER_BOX / 32;
             constexpr int BOXES = BN / COLS_PER_BOX;
+            // lane j's scale and bias of column j of the next chunk are loaded one chunk ahead
+            // (gemm_i8.cuh load_sb4): loaded at the chunk's start they cost an L2 round trip each
+            float sb_n = n0 + lane < N ? args.sb[n0 + lane] : 0.f;
+            float bias_n = (args.bias != nullptr && n0 + lane < N) ? args.bias[n0 + lane] : 0.f;
 #pragma unroll 1
             for (int bx = 0; bx < BOXES; ++bx, ++box_count) {
                 uint8_t* box = my_boxes + (box_count % S::BOX_BUFS) * S::BOX_BYTES;
@@ -295,9 +305,12 @@ gemm_i8_streamk_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_
 #pragma unroll
                 for (int cc = 0; cc < CHUNKS_PER_BOX; ++cc) {
                     const int col0 = bx * COLS_PER_BOX + cc * 32;
-                    const int gcol = n0 + col0 + lane;
-                    const float sb_l = gcol < N ? args.sb[gcol] : 0.f;
-                    const float bias_l = (args.bias != nullptr && gcol < N) ? args.bias[gcol] : 0.f;
+                    const float sb_l = sb_n, bias_l = bias_n;
+                    const int ncol = n0 + col0 + 32 + lane;
+                    if (col0 + 32 < BN) {
+                        sb_n = ncol < N ? args.sb[ncol] : 0.f;
+                        bias_n = (args.bias != nullptr && ncol < N) ? args.bias[ncol] : 0.f;
+                    }
                     uint32_t r[32];
                     tmem_ld_32x32b_x32(t_row + col0, r);
                     if (finish) {
