@@ -585,9 +585,10 @@ def run_prefill(dev, rank, world, batch_tokens=16384):
     del pf_m
     # config 4: 256 requests sharded over the ranks; each rank scores its share in batches of
     # similar length (sorted, padded to 64-token buckets, up to batch_tokens rows per pass)
-    from mica_b200.shard import lpt_shard, per_rank, plan_batches
+    from mica_b200.shard import balanced_shard, per_rank, plan_batches, plan_cost
     lengths, n_opts, req_ids = request_set()
-    mine = lpt_shard(lengths, world, rank)
+    mine = balanced_shard(lengths, world, rank, batch_tokens)
+    modelled = plan_cost([int(lengths[i]) for i in mine], batch_tokens)
     batches = plan_batches([int(lengths[i]) for i in mine], batch_tokens)
     dev_ids = {i: torch.from_numpy(req_ids[i]).to(dev) for i in mine}
 
@@ -609,16 +610,21 @@ def run_prefill(dev, rank, world, batch_tokens=16384):
     run_batches()
     b.record()
     b.synchronize()
-    busy = [r[0] for r in per_rank([a.elapsed_time(b)], dev)]
+    per = per_rank([a.elapsed_time(b), modelled], dev)
+    busy = [r[0] for r in per]
+    model_cost = [r[1] for r in per]
     ms_box = max(busy)
     total = int(lengths.sum())
     out['config4_batch256'] = {'requests': len(lengths), 'tokens': total, 'ms_box': round(ms_box, 1),
                                'tokens_per_s_box': round(total / ms_box * 1e3),
                                'busy_ms_per_rank': [round(v, 1) for v in busy],
                                'busy_max_over_mean': round(max(busy) / (sum(busy) / len(busy)), 4),
+                               'modelled_cost_per_rank': [round(v) for v in model_cost],
+                               'modelled_max_over_mean': round(max(model_cost) / (sum(model_cost) / len(model_cost)), 4),
                                'batches_rank0': len(batches), 'batch_graphs_rank0': len(shapes),
                                'batch_tokens': batch_tokens,
-                               'sharding': f'LPT over {world} ranks, no collective'}
+                               'sharding': f'LPT refined against each rank\'s batch plan (shard.balanced_shard) '
+                                           f'over {world} ranks, no collective'}
     pf.release()
     del model, pf
     torch.cuda.empty_cache()

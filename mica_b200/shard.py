@@ -15,6 +15,8 @@ or gloo on CPU); the kernels themselves are single-GPU.
 """
 from __future__ import annotations
 
+import functools
+
 
 def request_cost(length: int) -> float:
     """Relative prefill cost of one request: linears ~ L, causal attention ~ L^2 (the 4B
@@ -40,18 +42,30 @@ def lpt_shard(lengths, world: int, rank: int) -> list:
     return sorted(mine)
 
 
-# Fixed cost of one more batch (36 layers of launches, ramp-ups and tails), in tokens of work.
-# Fitted on B200 from two plans of the 256-request set: 34 batches with 6.0 % padding ran at
-# 178.6 K tokens/s and 52 batches with 2.1 % padding at 180.9 K, which puts one batch at ~625 tokens.
+# Cost of one padded [B, L] batch of the 4B model in "tokens of linear work":
+#   B * L                      the projections and MLP (per token),
+#   B * L * L / ATT_CROSS      causal attention (per token, growing with L),
+#   BATCH_COST_TOKENS          a fixed cost per batch (36 layers of launches, ramp-ups, tails).
+# The constants are refitted on B200 by timing batches through the same graph path config 4 runs.
+ATT_CROSS = 8192.0
 BATCH_COST_TOKENS = 640
 
 
-def plan_batches(lengths, batch_tokens: int, bucket: int = 64, batch_cost: int = BATCH_COST_TOKENS) -> list:
+def batch_cost(B: int, L: int, att_cross: float = ATT_CROSS, fixed: float = BATCH_COST_TOKENS) -> float:
+    """Modelled cost of one padded [B, L] batch (see above)."""
+    return float(B) * float(L) * (1.0 + float(L) / att_cross) + float(fixed)
+
+
+def plan_batches(lengths, batch_tokens: int, bucket: int = 64, batch_cost_tokens: float = BATCH_COST_TOKENS,
+                 att_cross: float = ATT_CROSS) -> list:
     """Groups request indices (into `lengths`) into padded [B, L] batches: contiguous runs of
     the length-sorted requests, L = the longest rounded up to `bucket`, B x L <= batch_tokens
-    (a longer request goes alone). Among all such partitions it returns one that minimises the
-    rows computed (sum of B x L, padding included) plus `batch_cost` per batch: an exact
-    dynamic program over the sorted order, O(n^2) for n requests."""
+    (a longer request goes alone). Among all such partitions it returns one of least total
+    batch_cost (padding included): an exact dynamic program over the sorted order, O(n^2)."""
+    return _plan(lengths, batch_tokens, bucket, batch_cost_tokens, att_cross)[0]
+
+
+def _plan(lengths, batch_tokens, bucket, fixed, att_cross):
     order = sorted(range(len(lengths)), key=lambda i: (lengths[i], i))
     n = len(order)
     pad = [-(-int(lengths[i]) // bucket) * bucket for i in order]
@@ -63,14 +77,70 @@ def plan_batches(lengths, batch_tokens: int, bucket: int = 64, batch_cost: int =
         for i in range(j - 1, -1, -1):
             if j - i > 1 and (j - i) * L > batch_tokens:
                 break
-            c = best[i] + (j - i) * L + batch_cost
+            c = best[i] + batch_cost(j - i, L, att_cross, fixed)
             if c < best[j]:
                 best[j], cut[j] = c, i
     out, j = [], n
     while j > 0:
         out.append([order[k] for k in range(cut[j], j)])
         j = cut[j]
-    return out[::-1]
+    return out[::-1], best[n]
+
+
+def plan_cost(lengths, batch_tokens: int, bucket: int = 64) -> float:
+    """Modelled cost of scoring `lengths` as plan_batches would batch them."""
+    return _plan_cost_sorted(tuple(sorted(int(x) for x in lengths)), batch_tokens, bucket)
+
+
+@functools.lru_cache(maxsize=65536)
+def _plan_cost_sorted(lengths: tuple, batch_tokens: int, bucket: int) -> float:
+    return _plan(list(lengths), batch_tokens, bucket, BATCH_COST_TOKENS, ATT_CROSS)[1] if lengths else 0.0
+
+
+def balanced_shard(lengths, world: int, rank: int, batch_tokens: int, max_rounds: int = 64) -> list:
+    """lpt_shard refined against each rank's batch plan: LPT balances per-request costs, but a
+    rank's time is its batches' (padding to each batch's longest, one fixed cost per batch).
+    Starting from LPT, it repeatedly moves one request from the rank of largest plan_cost to the
+    rank of least, or swaps one pair between them, taking the change that lowers the larger of
+    the two the most among the 48 that move nearest half the gap (by request_cost); it stops
+    when none lowers it (or after max_rounds). Deterministic,
+    so every rank derives the same plan. Returns this rank's request indices, ascending."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f'rank {rank} of world {world}')
+    return list(_balanced(tuple(int(x) for x in lengths), world, batch_tokens, max_rounds)[rank])
+
+
+@functools.lru_cache(maxsize=16)
+def _balanced(L: tuple, world: int, batch_tokens: int, max_rounds: int) -> tuple:
+    shards = [lpt_shard(L, world, r) for r in range(world)]
+    if world > 1:
+        cost = [plan_cost([L[i] for i in sh], batch_tokens) for sh in shards]
+        for _ in range(max_rounds):
+            hi = max(range(world), key=lambda r: (cost[r], -r))
+            lo = min(range(world), key=lambda r: (cost[r], r))
+            if hi == lo:
+                break
+            gap = cost[hi] - cost[lo]
+            best = (cost[hi], None)
+            a, b = shards[hi], shards[lo]
+            # a change helps when it moves between 0 and `gap` of work; try the 48 whose per-request
+            # cost moved is nearest half the gap (each try costs two plan evaluations)
+            cands = [(abs(request_cost(L[i]) - gap / 2), i, -1) for i in a if request_cost(L[i]) < gap]
+            cands += [(abs(request_cost(L[i]) - request_cost(L[j]) - gap / 2), i, j) for i in a for j in b
+                      if 0.0 < request_cost(L[i]) - request_cost(L[j]) < gap]
+            cands.sort()
+            for _, i, j in cands[:48]:
+                out_, in_ = [i], ([j] if j >= 0 else [])
+                na = [i for i in a if i not in out_] + in_
+                nb = [j for j in b if j not in in_] + out_
+                ca = plan_cost([L[i] for i in na], batch_tokens)
+                cb = plan_cost([L[j] for j in nb], batch_tokens)
+                if max(ca, cb) < best[0] - 1e-9:
+                    best = (max(ca, cb), (sorted(na), sorted(nb), ca, cb))
+            if best[1] is None:
+                break
+            shards[hi], shards[lo], cost[hi], cost[lo] = best[1]
+    return tuple(tuple(sorted(sh)) for sh in shards)
 
 
 def max_over_ranks(values, device='cpu'):

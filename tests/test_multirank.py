@@ -94,15 +94,18 @@ def test_two_gloo_ranks_partition_reduce_and_gather(tmp_path):
             assert len(b) == 1 or len(b) * pad <= 16384
 
 
-def test_batch_plan_minimises_padded_rows_plus_batch_cost():
-    """The planner's partition is never worse, on its own objective, than the greedy fill of
-    each batch up to the token budget, and respects the budget."""
+def test_batch_plan_minimises_modelled_batch_cost():
+    """The planner's partition is never worse, on its own objective (padded rows, their
+    attention term and a fixed cost per batch), than the greedy fill of each batch up to the
+    token budget, and respects the budget."""
     lengths = _lengths(n=200, seed=11)
     plan = SH.plan_batches(lengths, 16384)
     assert sorted(i for b in plan for i in b) == list(range(len(lengths)))
 
     def cost(batches):
-        return sum(len(b) * (-(-max(lengths[i] for i in b) // 64) * 64) + SH.BATCH_COST_TOKENS for b in batches)
+        return sum(SH.batch_cost(len(b), -(-max(lengths[i] for i in b) // 64) * 64) for b in batches)
+
+    assert abs(cost(plan) - SH.plan_cost(lengths, 16384)) < 1e-6 * cost(plan)
 
     order = sorted(range(len(lengths)), key=lambda i: (lengths[i], i))
     greedy, cur = [], []
@@ -158,3 +161,23 @@ def test_plan_edge_cases():
     assert sorted(i for b in plan for i in b) == [0, 1, 2] and [0] in plan
     shares = [SH.lpt_shard([300, 5000], 4, r) for r in range(4)]
     assert sorted(i for s in shares for i in s) == [0, 1] and sum(1 for s in shares if not s) == 2
+
+
+def test_balanced_shard_refines_lpt_against_the_batch_plans():
+    """Every request lands on exactly one rank, every rank derives the same split, and the
+    slowest rank's modelled plan cost is never above LPT's (the BASELINE config-4 set: 256
+    lognormal requests, 8 ranks)."""
+    lengths = _lengths(n=256, seed=3)
+    for world in (2, 4, 8):
+        bal = [SH.balanced_shard(lengths, world, r, 16384) for r in range(world)]
+        assert sorted(i for sh in bal for i in sh) == list(range(len(lengths)))
+        assert bal == [SH.balanced_shard(lengths, world, r, 16384) for r in range(world)]
+        lpt = [SH.lpt_shard(lengths, world, r) for r in range(world)]
+        worst = lambda shards: max(SH.plan_cost([lengths[i] for i in sh], 16384) for sh in shards)  # noqa: E731
+        assert worst(bal) <= worst(lpt) + 1e-6
+    assert SH.balanced_shard(lengths, 1, 0, 16384) == list(range(len(lengths)))
+    assert SH.balanced_shard([], 4, 2, 16384) == []
+    shares = [SH.balanced_shard([300, 5000], 4, r, 16384) for r in range(4)]
+    assert sorted(i for s in shares for i in s) == [0, 1]
+    with pytest.raises(ValueError):
+        SH.balanced_shard(lengths, 2, 2, 16384)
