@@ -87,7 +87,7 @@ typedef struct mica_caps {
     int pair_clusters;      /* co-resident CTA pairs for the 256-row GEMM tiles         */
 } mica_caps;
 
-#define MICA_ABI_VERSION 4
+#define MICA_ABI_VERSION 5
 
 /* Capability query. Replaces int8_kernels.available() (v0.5/serving/lib/int8_kernels.py:146-159)
  * and the capability probe in _device_cc (:130-143). Fills *caps for `device`.         */

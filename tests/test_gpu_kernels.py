@@ -557,3 +557,36 @@ def test_gemm_wide_tile_needs_one_wave(K):
                                     y.data_ptr(), 0, n, m, n, k, 128, 320, 0, 0, st)
     assert rc == 8                                   # MICA_ERR_UNSUPPORTED
     assert dev_error() == 0
+
+
+def test_automatic_width_keeps_256_when_the_caller_forces_a_split_or_caps_the_grid(K):
+    """Config 0's shape (M 512, N 9728, K 2560) is where the library choice takes 128 x 320
+    tiles. With the width left to the library but a forced cluster split, a forced stream-K or
+    a grid cap below one wave, it must keep a 256-wide path: a 320-wide choice would refuse
+    each of these (MICA_ERR_UNSUPPORTED). Every form is bit-exact against the oracle."""
+    from mica_b200 import _native as N
+    lib = N.lib()
+    m, n, k = 512, 9728, 2560
+    g = torch.Generator().manual_seed(512)
+    qx = torch.randint(-31, 32, (m, k), generator=g, dtype=torch.int8)
+    qw = torch.randint(-31, 32, (n, k), generator=g, dtype=torch.int8)
+    acc = O.int_gemm_exact(qx.numpy(), qw.numpy()).astype(np.int64)
+    qxc, qwc = qx.cuda(), qw.cuda()
+    ones = torch.ones(max(m, n), device='cuda')
+    st = torch.cuda.current_stream().cuda_stream
+    F32 = 2
+    for max_ctas, splits in ((0, 2), (0, 4), (100, 0), (0, 1)):
+        y = torch.full((m, n), -1.0, dtype=torch.float32, device='cuda')
+        rc = lib.mica_w8a8_gemm_cfg(qxc.data_ptr(), k, qwc.data_ptr(), k, ones.data_ptr(), ones.data_ptr(), None,
+                                    y.data_ptr(), F32, n, m, n, k, 0, 0, max_ctas, splits, st)
+        assert rc == 0, (max_ctas, splits, rc)
+        assert np.array_equal(y.cpu().numpy().astype(np.int64), acc), (max_ctas, splits)
+    need = lib.mica_w8a8_gemm_workspace_bytes(m, n, k, 0, 0, 0, -1)
+    assert need > 0                                  # stream-K planned: a 256- or 128-wide tile
+    ws = torch.empty(need, dtype=torch.uint8, device='cuda')
+    y = torch.full((m, n), -1.0, dtype=torch.float32, device='cuda')
+    rc = lib.mica_w8a8_gemm_ex(qxc.data_ptr(), k, qwc.data_ptr(), k, ones.data_ptr(), ones.data_ptr(), None,
+                               y.data_ptr(), F32, n, m, n, k, 0, 0, 0, -1, ws.data_ptr(), need, st)
+    assert rc == 0
+    assert np.array_equal(y.cpu().numpy().astype(np.int64), acc)
+    assert dev_error() == 0
