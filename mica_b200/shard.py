@@ -20,8 +20,8 @@ import functools
 
 def request_cost(length: int) -> float:
     """Relative prefill cost of one request: linears ~ L, causal attention ~ L^2 (the 4B
-    model's two terms cross near L = 8192)."""
-    return float(length) + float(length) * float(length) / 8192.0
+    model's two terms cross near L = ATT_CROSS)."""
+    return float(length) + float(length) * float(length) / ATT_CROSS
 
 
 def lpt_shard(lengths, world: int, rank: int) -> list:
@@ -45,10 +45,12 @@ def lpt_shard(lengths, world: int, rank: int) -> list:
 # Cost of one padded [B, L] batch of the 4B model in "tokens of linear work":
 #   B * L                      the projections and MLP (per token),
 #   B * L * L / ATT_CROSS      causal attention (per token, growing with L),
-#   BATCH_COST_TOKENS          a fixed cost per batch (36 layers of launches, ramp-ups, tails).
-# The constants are refitted on B200 by timing batches through the same graph path config 4 runs.
-ATT_CROSS = 8192.0
-BATCH_COST_TOKENS = 640
+#   BATCH_COST_TOKENS          a fixed cost per batch (36 layers of small-M GEMM floors, launches).
+# Fitted on B200 (least squares on relative error) to 15 batch shapes from [1, 256] to [1, 32768]
+# and [64, 256], timed through the captured batch graphs config 4 replays: 3.63 us per token,
+# 0.218 ns per token per key, 4.37 ms per batch; every shape within 5 % of the fit.
+ATT_CROSS = 16600.0
+BATCH_COST_TOKENS = 1200
 
 
 def batch_cost(B: int, L: int, att_cross: float = ATT_CROSS, fixed: float = BATCH_COST_TOKENS) -> float:
@@ -98,9 +100,10 @@ def _plan_cost_sorted(lengths: tuple, batch_tokens: int, bucket: int) -> float:
 
 
 def balanced_shard(lengths, world: int, rank: int, batch_tokens: int, max_rounds: int = 64) -> list:
-    """lpt_shard refined against each rank's batch plan: LPT balances per-request costs, but a
+    """Shares refined against each rank's batch plan: LPT balances per-request costs, but a
     rank's time is its batches' (padding to each batch's longest, one fixed cost per batch).
-    Starting from LPT, it repeatedly moves one request from the rank of largest plan_cost to the
+    Starting from the better (by that model) of lpt_shard and batch_first_shards, it repeatedly
+    moves one request from the rank of largest plan_cost to the
     rank of least, or swaps one pair between them, taking the change that lowers the larger of
     the two the most among the 48 that move nearest half the gap (by request_cost); it stops
     when none lowers it (or after max_rounds). Deterministic,
@@ -110,9 +113,31 @@ def balanced_shard(lengths, world: int, rank: int, batch_tokens: int, max_rounds
     return list(_balanced(tuple(int(x) for x in lengths), world, batch_tokens, max_rounds)[rank])
 
 
+def batch_first_shards(lengths, world: int, batch_tokens: int) -> list:
+    """All ranks' shares when the batches are planned over the whole request set (the plan one
+    GPU would run) and whole batches are dealt out by LPT on their modelled cost. Splitting a
+    length class across ranks costs extra batches, each a fixed cost; this keeps the batch
+    count of the single-GPU plan. Deterministic."""
+    L = [int(x) for x in lengths]
+    plan = plan_batches(L, batch_tokens)
+    costs = [batch_cost(len(b), -(-max(L[i] for i in b) // 64) * 64) for b in plan]
+    order = sorted(range(len(plan)), key=lambda k: (-costs[k], k))
+    load = [0.0] * world
+    shards = [[] for _ in range(world)]
+    for k in order:
+        r = min(range(world), key=lambda j: (load[j], j))
+        load[r] += costs[k]
+        shards[r].extend(plan[k])
+    return [sorted(sh) for sh in shards]
+
+
 @functools.lru_cache(maxsize=16)
 def _balanced(L: tuple, world: int, batch_tokens: int, max_rounds: int) -> tuple:
-    shards = [lpt_shard(L, world, r) for r in range(world)]
+    # start from whichever of request-level LPT and batch-first LPT leaves the slowest rank
+    # cheaper under the batch-plan model
+    starts = [[lpt_shard(L, world, r) for r in range(world)], batch_first_shards(L, world, batch_tokens)]
+    worst = [max(plan_cost([L[i] for i in sh], batch_tokens) for sh in st) for st in starts]
+    shards = [list(sh) for sh in starts[0 if worst[0] <= worst[1] else 1]]
     if world > 1:
         cost = [plan_cost([L[i] for i in sh], batch_tokens) for sh in shards]
         for _ in range(max_rounds):
