@@ -247,20 +247,28 @@ __device__ __forceinline__ void dequant_chunk(const GemmArgs& args, uint32_t t_a
 }
 
 // The SwiGLU epilogue's per-lane column values of one 32-column chunk at tile column col0: lane
-// j's gate/up scale and bias of column col0 + j, and down_proj's smoothing of h column
-// col0 / 2 + (j & 15). Loaded one chunk ahead of use, as load_sb4.
+// j's gate/up bias of column col0 + j and down_proj's smoothing of h column col0 / 2 + (j & 15),
+// each only when present (the scales come from the tile's shared-memory copy). Loaded one chunk
+// ahead of use.
 struct SwigluCols {
-    float sb, bias, inv;
+    float bias, inv;
 };
 __device__ __forceinline__ SwigluCols load_swiglu_cols(const GemmArgs& a, int gcol0, int N) {
     const int lane = threadIdx.x & 31;
     const int gcol = gcol0 + lane;
     const int hcol = gcol0 / 2 + (lane & 15);
     SwigluCols c;
-    c.sb = gcol < N ? a.sb[gcol] : 0.f;
     c.bias = (a.bias != nullptr && gcol < N) ? a.bias[gcol] : 0.f;
     c.inv = (a.inv_h != nullptr && hcol < N / 2) ? a.inv_h[hcol] : 1.f;
     return c;
+}
+
+// Two floats rounded to bf16 by one cvt.rn.bf16x2.f32 (each element RN, as a scalar cast) and
+// widened back; `packed` keeps the bf16 pair (lo in the low half).
+__device__ __forceinline__ void bf16_round2(float& lo, float& hi, uint32_t& packed) {
+    packed = pack_bf16(lo, hi);
+    lo = __uint_as_float(packed << 16);
+    hi = __uint_as_float(packed & 0xFFFF0000u);
 }
 
 // f[e] = RN(f[e] * inv[e]) for eight consecutive columns (inv 16-byte aligned).
@@ -488,14 +496,15 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
                 if (args.inv_h != nullptr && lane * 32 < BN / 2 && (n0 / 2) + lane * 32 < N / 2)
                     prefetch_l1(args.inv_h + n0 / 2 + lane * 32);
             }
-            // Dequant: the tile's BN column scales go to shared memory while the accumulator is
-            // computed (cols_free: every epilogue warp is done with the previous tile's; cols_full:
-            // all of this tile's are stored; one arrival per warp, bounded waits). Measured on B200, a chunk that loaded its scales at
+            // The tile's BN column scales go to shared memory while the accumulator is computed
+            // (cols_free: every epilogue warp is done with the previous tile's; cols_full: all of
+            // this tile's are stored; one arrival per warp, bounded waits). Measured on B200, a chunk that loaded its scales at
             // its own start waited ~450 cycles for L2, which on one-tile-per-CTA grids left ~1.4 us
             // of epilogue exposed per warp; the values do not stay in the small L1 beside 227 KB of
-            // shared memory. SwiGLU: the first chunk's per-lane values, loaded one chunk ahead.
+            // shared memory. SwiGLU also loads the first chunk's per-lane bias and smoothing values
+            // (when present), one chunk ahead.
             SwigluCols sw_cur;
-            if constexpr (EPI == EPI_DEQUANT) {
+            {
                 bool cw = true;
                 if (lane == 0 && local > 0)
                     cw = mbar_wait(cols_free, (local - 1) & 1, abort_flag, MICA_DEV_TIMEOUT_EPILOGUE);
@@ -509,8 +518,7 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
                 }
                 if (!__shfl_sync(0xffffffffu, cw, 0)) break;
                 __syncwarp();                  // orders the lanes' reads after lane 0's acquire
-            } else {
-                sw_cur = load_swiglu_cols(args, n0 + part * 128, N);
+                if constexpr (EPI == EPI_SWIGLU) sw_cur = load_swiglu_cols(args, n0 + part * 128, N);
             }
             bool w = true;
             if (lane == 0) w = mbar_wait(&tfull_bar[acc], acc_ph, abort_flag, MICA_DEV_TIMEOUT_EPILOGUE);
@@ -574,43 +582,52 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
 #pragma unroll
                     for (int cc = 0; cc < CHUNKS_PER_BOX; ++cc) {
                         const int col0 = bx * 128 + cc * 32;
-                        const float sb_l = sw_cur.sb, bias_l = sw_cur.bias;
+                        const float bias_l = sw_cur.bias;
                         const float inv_l = sw_cur.inv;   // down_proj's smoothing of h column (n0 + col0) / 2 + (lane & 15)
                         // this warp's next chunk's values, in flight while this chunk is processed
                         const int ncol = cc + 1 < CHUNKS_PER_BOX ? col0 + 32 : (bx + PARTS) * 128;
                         if (ncol < BN) sw_cur = load_swiglu_cols(args, n0 + ncol, N);
+                        // the chunk's 16 gate and 16 up scales: uniform shared loads, one broadcast each
+                        float4 sb4[8];
+#pragma unroll
+                        for (int v = 0; v < 8; ++v) sb4[v] = reinterpret_cast<const float4*>(smem_cols + col0)[v];
+                        const float* sbc = reinterpret_cast<const float*>(sb4);
                         uint32_t r[32];
                         tmem_ld_32x32b_x32(t_row + col0, r);
                         tmem_ld_wait();
                         uint32_t p[8];
 #pragma unroll
                         for (int j = 0; j < 16; j += 2) {
-                            float hv[2];
-#pragma unroll
-                            for (int e = 0; e < 2; ++e) {
-                                const int jj = j + e;
-                                float g = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[jj])), sa_v),
-                                                    __shfl_sync(0xffffffffu, sb_l, jj));
-                                float u = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[16 + jj])), sa_v),
-                                                    __shfl_sync(0xffffffffu, sb_l, 16 + jj));
-                                if (args.bias != nullptr) {
-                                    g = __fadd_rn(g, __shfl_sync(0xffffffffu, bias_l, jj));
-                                    u = __fadd_rn(u, __shfl_sync(0xffffffffu, bias_l, 16 + jj));
-                                }
-                                g = bf16_round(g);
-                                u = bf16_round(u);
-                                // silu in fp32 with branch-free intrinsics (few-ulp fp32 error,
-                                // below the bf16 rounding that follows), so the 16 independent
-                                // chains of a chunk interleave instead of serialising on slow paths
-                                const float act = bf16_round(__fdividef(g, 1.0f + __expf(-g)));
-                                const float h = bf16_round(__fmul_rn(act, u));
-                                // the requant's input is RN(h * inv) (act_quant's xf * inv_smooth)
-                                const float hs = args.inv_h != nullptr
-                                                     ? __fmul_rn(h, __shfl_sync(0xffffffffu, inv_l, jj)) : h;
-                                amax = fmaxf(amax, fabsf(hs));
-                                hv[e] = h;
+                            // outputs j and j + 1: g, u dequantised, each rounded to bf16 (the two
+                            // QLinears' outputs), silu(g) rounded, h = bf16(silu(g) * u); the
+                            // roundings run on pairs
+                            float g0 = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[j])), sa_v), sbc[j]);
+                            float g1 = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[j + 1])), sa_v), sbc[j + 1]);
+                            float u0 = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[16 + j])), sa_v), sbc[16 + j]);
+                            float u1 = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(r[17 + j])), sa_v), sbc[17 + j]);
+                            if (args.bias != nullptr) {
+                                g0 = __fadd_rn(g0, __shfl_sync(0xffffffffu, bias_l, j));
+                                g1 = __fadd_rn(g1, __shfl_sync(0xffffffffu, bias_l, j + 1));
+                                u0 = __fadd_rn(u0, __shfl_sync(0xffffffffu, bias_l, 16 + j));
+                                u1 = __fadd_rn(u1, __shfl_sync(0xffffffffu, bias_l, 17 + j));
                             }
-                            p[j / 2] = pack_bf16(hv[0], hv[1]);
+                            uint32_t pk;
+                            bf16_round2(g0, g1, pk);
+                            bf16_round2(u0, u1, pk);
+                            // silu in fp32 with branch-free intrinsics (few-ulp fp32 error, below
+                            // the bf16 rounding that follows), so the 16 independent chains of a
+                            // chunk interleave instead of serialising on slow paths
+                            float a0 = __fdividef(g0, 1.0f + __expf(-g0));
+                            float a1 = __fdividef(g1, 1.0f + __expf(-g1));
+                            bf16_round2(a0, a1, pk);
+                            float h0 = __fmul_rn(a0, u0), h1 = __fmul_rn(a1, u1);
+                            bf16_round2(h0, h1, p[j / 2]);
+                            // the requant's input is RN(h * inv) (act_quant's xf * inv_smooth)
+                            if (args.inv_h != nullptr) {
+                                h0 = __fmul_rn(h0, __shfl_sync(0xffffffffu, inv_l, j));
+                                h1 = __fmul_rn(h1, __shfl_sync(0xffffffffu, inv_l, j + 1));
+                            }
+                            amax = fmaxf(fmaxf(amax, fabsf(h0)), fabsf(h1));
                         }
 #pragma unroll
                         for (int c = 0; c < 2; ++c) {
@@ -622,6 +639,7 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
                     if (bx + PARTS >= BOXES) {
                         tc_fence_before();
                         mbar_arrive(&tempty_bar[acc]);
+                        if (lane == 0) mbar_arrive(cols_free);   // and its last read of the scales
                     }
                     fence_proxy_async_smem();
                     __syncwarp();
@@ -630,6 +648,12 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant
                         if (x < N / 2 && y < M) tma_store_2d(&tmap_c, box, x, y);
                         tma_store_commit();
                     }
+                }
+                if (part >= BOXES) {
+                    // no box of this tile for this warp (BN = 128: one box, two warps per lane
+                    // quarter): it reads neither the accumulator nor the scales, and hands both back
+                    mbar_arrive(&tempty_bar[acc]);
+                    if (lane == 0) mbar_arrive(cols_free);
                 }
                 if (grow < M) atomicMax(args.row_amax + grow, __float_as_uint(amax));
             }
