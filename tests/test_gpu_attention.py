@@ -21,7 +21,8 @@ def _reference(qkv, B, L, H, KV, D, scale):
 
 
 @pytest.mark.parametrize('B,L,H,KV', [(1, 128, 4, 2), (1, 333, 32, 8), (2, 256, 8, 8), (3, 200, 16, 4),
-                                      (1, 2048, 32, 8), (2, 1000, 4, 1)])
+                                      (1, 2048, 32, 8), (2, 1000, 4, 1), (1, 1, 8, 2), (2, 127, 4, 4),
+                                      (1, 129, 4, 2), (3, 257, 8, 2)])
 def test_attention_matches_fp32_reference(B, L, H, KV):
     from mica_b200 import ops  # noqa: F401
     D = 128
@@ -62,3 +63,15 @@ def test_attention_rejects_bad_arguments():
     assert lib.mica_attention_prefill(buf.data_ptr(), 1536, buf.data_ptr(), 1024, 1, 8, 8, 3, 128, 0.1, st) == 2  # H % KV
     assert lib.mica_attention_prefill(buf.data_ptr(), 1536, buf.data_ptr(), 1024, 1, 8, 8, 2, 64, 0.1, st) == 2   # D
     assert lib.mica_attention_prefill(buf.data_ptr(), 1535, buf.data_ptr(), 1024, 1, 8, 4, 2, 128, 0.1, st) == 3  # stride
+
+
+def test_attention_of_an_empty_batch_is_a_no_op():
+    """B = 0 or L = 0: nothing to compute; the call succeeds and launches nothing."""
+    from mica_b200 import _native as N
+    lib = N.lib()
+    buf = torch.zeros(16, dtype=torch.bfloat16, device='cuda')
+    st = torch.cuda.current_stream().cuda_stream
+    assert lib.mica_attention_prefill(buf.data_ptr(), 1536, buf.data_ptr(), 1024, 0, 8, 8, 2, 128, 0.1, st) == 0
+    assert lib.mica_attention_prefill(buf.data_ptr(), 1536, buf.data_ptr(), 1024, 2, 0, 8, 2, 128, 0.1, st) == 0
+    torch.cuda.synchronize()
+    assert float(buf.float().abs().sum()) == 0.0
